@@ -1,0 +1,323 @@
+"""Python mirror of Aegaeon's ``aegaeon.ops`` operator module, backed by the sm_100a C ABI.
+
+``swap`` keeps the exact call signature and meaning of the reference operator
+(``aegaeon/ops/ops.h:4-10``, ``aegaeon/ops/swap.cu:25-60``): it runs on the current torch stream,
+returns before the copy completes, and takes the block geometry from ``kv_cache``. The other
+operators are the per-layer cache write and decode attention that the reference reaches through
+vLLM 0.5.1 (``aegaeon/aegaeon/worker.py:517-523``) and the block copy of vLLM's cache ops, on
+Aegaeon's ``(N, L, 2, 16, Hkv, D)`` block layout.
+
+Every operator validates its arguments on the host and raises ``ValueError`` (bad argument),
+``NotImplementedError`` (unsupported shape) or ``AegaeonError`` (CUDA failure). There is no CPU
+or PyTorch fallback: the work always runs in the CUDA library.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _native
+from ._native import check, lib
+from .layout import BLOCK_SIZE, block_bytes
+
+_DTYPES = {torch.float16: _native.AEG_DTYPE_FP16, torch.bfloat16: _native.AEG_DTYPE_BF16}
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+def _ids_array(ids, name: str) -> np.ndarray:
+    if isinstance(ids, torch.Tensor):
+        ids = ids.detach().cpu().numpy()
+    arr = np.ascontiguousarray(np.asarray(ids, dtype=np.int64).reshape(-1))
+    return arr
+
+
+def _device_ids(ids, device: torch.device, name: str) -> torch.Tensor:
+    if isinstance(ids, torch.Tensor):
+        if ids.dtype != torch.int64:
+            ids = ids.to(torch.int64)
+        return ids.to(device, non_blocking=True).contiguous().view(-1)
+    return torch.as_tensor(np.asarray(ids, dtype=np.int64).reshape(-1)).to(device, non_blocking=True)
+
+
+def read_device_errors(device: torch.device | int | None = None) -> int:
+    """Reads and clears the library's sticky device error bits (synchronises the stream)."""
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    if isinstance(device, int):
+        dev = torch.device("cuda", device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    flags = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        check(lib.aeg_read_device_errors(_stream(dev), ctypes.byref(flags)), "read_device_errors")
+    return int(flags.value)
+
+
+# --------------------------------------------------------------------------------------------
+# Block movement
+
+
+def _check_pools(kv_cache: torch.Tensor, kv_swap: torch.Tensor) -> int:
+    _require_cuda(kv_cache, "kv_cache")
+    if not isinstance(kv_swap, torch.Tensor) or kv_swap.device.type != "cpu":
+        raise ValueError("kv_swap must be a CPU (host) tensor")
+    if not kv_cache.is_contiguous() or not kv_swap.is_contiguous():
+        raise ValueError("kv_cache and kv_swap must be contiguous")
+    bb = block_bytes(kv_cache)
+    if kv_swap.dim() > 0 and kv_swap.size(0) > 0:
+        host_bb = kv_swap.numel() * kv_swap.element_size() // kv_swap.size(0)
+        if host_bb != bb:
+            raise ValueError(f"kv_swap block of {host_bb} bytes differs from kv_cache block of {bb} bytes")
+    return bb
+
+
+def swap(source_block_ids: Sequence[int], target_block_ids: Sequence[int], is_swap_in: bool,
+         kv_cache: torch.Tensor, kv_swap: torch.Tensor) -> None:
+    """Copies whole KV blocks between the device cache and the host swap pool.
+
+    ``is_swap_in``: host block ``source_block_ids[i]`` -> device block ``target_block_ids[i]``;
+    otherwise device -> host. Enqueued on the current stream of ``kv_cache``'s device.
+    """
+    src = _ids_array(source_block_ids, "source_block_ids")
+    dst = _ids_array(target_block_ids, "target_block_ids")
+    if src.shape != dst.shape:
+        raise ValueError(f"{src.size} source ids but {dst.size} target ids")
+    bb = _check_pools(kv_cache, kv_swap)
+    if src.size == 0:
+        return
+    n_host = kv_swap.size(0) if kv_swap.dim() > 0 else 0
+    with torch.cuda.device(kv_cache.device):
+        st = lib.aeg_swap(kv_cache.data_ptr(), kv_swap.data_ptr(), bb, kv_cache.size(0), n_host,
+                          src.ctypes.data, dst.ctypes.data, src.size, int(bool(is_swap_in)),
+                          _stream(kv_cache.device))
+    check(st, "swap")
+
+
+def swap_sm(source_block_ids, target_block_ids, is_swap_in: bool, kv_cache: torch.Tensor,
+            kv_swap: torch.Tensor) -> None:
+    """``swap`` done by one kernel over the mapped page-locked host pool (scattered ids, one launch).
+
+    ``kv_swap`` must be page-locked (``pin_memory()`` or ``cudaHostRegister``). Ids may be lists or
+    int64 tensors; they are staged to the device on the current stream.
+    """
+    bb = _check_pools(kv_cache, kv_swap)
+    dev = kv_cache.device
+    src = _device_ids(source_block_ids, dev, "source_block_ids")
+    dst = _device_ids(target_block_ids, dev, "target_block_ids")
+    if src.numel() != dst.numel():
+        raise ValueError(f"{src.numel()} source ids but {dst.numel()} target ids")
+    if src.numel() == 0:
+        return
+    n_host = kv_swap.size(0) if kv_swap.dim() > 0 else 0
+    with torch.cuda.device(dev):
+        st = lib.aeg_swap_sm(kv_cache.data_ptr(), kv_swap.data_ptr(), bb, kv_cache.size(0), n_host,
+                             src.data_ptr(), dst.data_ptr(), src.numel(), int(bool(is_swap_in)), _stream(dev))
+    check(st, "swap_sm")
+    # keep the staged id tensors alive until the kernel has consumed them
+    src.record_stream(torch.cuda.current_stream(dev))
+    dst.record_stream(torch.cuda.current_stream(dev))
+
+
+def copy_blocks(src_ids, dst_ids, kv_cache: torch.Tensor) -> None:
+    """``kv_cache[dst_ids[i]] = kv_cache[src_ids[i]]`` for whole multi-layer blocks (device to device)."""
+    _require_cuda(kv_cache, "kv_cache")
+    if not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be contiguous")
+    dev = kv_cache.device
+    src = _device_ids(src_ids, dev, "src_ids")
+    dst = _device_ids(dst_ids, dev, "dst_ids")
+    if src.numel() != dst.numel():
+        raise ValueError(f"{src.numel()} source ids but {dst.numel()} destination ids")
+    if src.numel() == 0:
+        return
+    with torch.cuda.device(dev):
+        st = lib.aeg_copy_blocks(kv_cache.data_ptr(), block_bytes(kv_cache), kv_cache.size(0), src.data_ptr(),
+                                 dst.data_ptr(), src.numel(), _stream(dev))
+    check(st, "copy_blocks")
+    src.record_stream(torch.cuda.current_stream(dev))
+    dst.record_stream(torch.cuda.current_stream(dev))
+
+
+# --------------------------------------------------------------------------------------------
+# Per-layer cache write
+
+
+def _layer_views(kv_cache: torch.Tensor, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda(kv_cache, "kv_cache")
+    if kv_cache.dim() != 6 or kv_cache.size(2) != 2 or kv_cache.size(3) != BLOCK_SIZE:
+        raise ValueError(f"kv_cache must have shape (N, L, 2, 16, Hkv, D), got {tuple(kv_cache.shape)}")
+    if not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be contiguous")
+    if not 0 <= layer < kv_cache.size(1):
+        raise ValueError(f"layer {layer} outside [0, {kv_cache.size(1)})")
+    return kv_cache[:, layer, 0], kv_cache[:, layer, 1]
+
+
+def _check_paged_view(t: torch.Tensor, name: str) -> None:
+    _require_cuda(t, name)
+    if t.dim() != 4 or t.size(1) != BLOCK_SIZE:
+        raise ValueError(f"{name} must be (N, 16, Hkv, D), got {tuple(t.shape)}")
+    Hkv, D = t.size(2), t.size(3)
+    if t.stride(3) != 1 or t.stride(2) != D or t.stride(1) != Hkv * D:
+        raise ValueError(f"{name} must have a contiguous (16, Hkv, D) block interior")
+
+
+def reshape_and_cache_flash(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
+                            value_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                            kv_cache_dtype: str = "auto") -> None:
+    """vLLM-shaped cache write: ``key_cache[s // 16, s % 16] = key[t]`` (same for value), s = slot_mapping[t] >= 0."""
+    if kv_cache_dtype != "auto":
+        raise NotImplementedError("only kv_cache_dtype='auto' (cache dtype == key dtype) is supported")
+    _check_paged_view(key_cache, "key_cache")
+    _check_paged_view(value_cache, "value_cache")
+    for name, t in (("key", key), ("value", value)):
+        _require_cuda(t, name)
+        if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.size(2):
+            raise ValueError(f"{name} must be [T, Hkv, D] with contiguous heads")
+        if t.dtype != key_cache.dtype:
+            raise ValueError(f"{name} dtype {t.dtype} differs from cache dtype {key_cache.dtype}")
+    if key.shape != value.shape or key.shape[1:] != key_cache.shape[2:]:
+        raise ValueError("key/value shapes do not match the cache (Hkv, D)")
+    if key_cache.shape != value_cache.shape or key_cache.stride() != value_cache.stride():
+        raise ValueError("key_cache and value_cache must have the same shape and strides")
+    _require_cuda(slot_mapping, "slot_mapping")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.numel() != key.size(0):
+        raise ValueError("slot_mapping must be int64 [T]")
+    if key.element_size() != 2:
+        raise NotImplementedError("only 2-byte cache elements (fp16/bf16) are supported")
+    slot_mapping = slot_mapping.contiguous()
+    dev = key_cache.device
+    with torch.cuda.device(dev):
+        st = lib.aeg_reshape_and_cache(key.data_ptr(), value.data_ptr(), key.stride(0), value.stride(0),
+                                       key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0),
+                                       key_cache.size(0), slot_mapping.data_ptr(), key.size(0), key.size(1),
+                                       key.size(2), _stream(dev))
+    check(st, "reshape_and_cache")
+
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor, layer: int,
+                      slot_mapping: torch.Tensor) -> None:
+    """Writes the new tokens' K/V of ``layer`` into Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache."""
+    kc, vc = _layer_views(kv_cache, layer)
+    reshape_and_cache_flash(key, value, kc, vc, slot_mapping)
+
+
+# --------------------------------------------------------------------------------------------
+# Decode attention
+
+
+class DecodePlan:
+    """Per-step work plan + scratch for ``paged_attention_decode`` (built once, used by every layer).
+
+    The plan depends only on ``seq_lens`` (like the per-step attention metadata of
+    ``aegaeon/aegaeon/worker.py:694-711``). Its workspace is device memory owned by this object;
+    one plan must not be used by two streams at the same time.
+    """
+
+    def __init__(self, batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                 device: torch.device | str = "cuda"):
+        self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim = batch, num_q_heads, num_kv_heads, head_dim
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DecodePlan needs a CUDA device")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        nbytes = lib.aeg_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim)
+        if nbytes == 0:
+            raise ValueError(f"invalid decode shape B={batch} Hq={num_q_heads} Hkv={num_kv_heads} D={head_dim}")
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.table_width: int | None = None
+        self.seq_lens: torch.Tensor | None = None
+
+    def plan(self, seq_lens: torch.Tensor, table_width: int) -> "DecodePlan":
+        """Builds the unit list for ``seq_lens`` (int32 CUDA [B]) on the current stream."""
+        _require_cuda(seq_lens, "seq_lens")
+        if seq_lens.dtype != torch.int32 or seq_lens.dim() != 1 or seq_lens.numel() != self.batch:
+            raise ValueError(f"seq_lens must be int32 [{self.batch}]")
+        seq_lens = seq_lens.contiguous()
+        with torch.cuda.device(self.device):
+            st = lib.aeg_decode_plan(self.workspace.data_ptr(), self.workspace.numel(), seq_lens.data_ptr(),
+                                     self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim, table_width,
+                                     _stream(self.device))
+        check(st, "decode_plan")
+        self.table_width = table_width
+        self.seq_lens = seq_lens
+        return self
+
+
+def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                      block_table: torch.Tensor, cache_seqlens: torch.Tensor, softmax_scale: float | None = None,
+                      out: torch.Tensor | None = None, plan: DecodePlan | None = None) -> torch.Tensor:
+    """Paged decode attention with one query token per sequence (vLLM FlashAttention decode call).
+
+    query ``[B, Hq, D]``; key_cache/value_cache ``(N, 16, Hkv, D)`` views (any block stride);
+    block_table int32 ``[B, W]``; cache_seqlens int32 ``[B]``. Returns ``out [B, Hq, D]``.
+    ``plan`` must have been built for these ``cache_seqlens`` and ``W``; without one a plan is built
+    on the fly (an extra launch).
+    """
+    _require_cuda(query, "query")
+    if query.dim() != 3 or query.stride(2) != 1 or query.stride(1) != query.size(2):
+        raise ValueError("query must be [B, Hq, D] with contiguous heads")
+    _check_paged_view(key_cache, "key_cache")
+    _check_paged_view(value_cache, "value_cache")
+    if key_cache.shape != value_cache.shape or key_cache.stride() != value_cache.stride():
+        raise ValueError("key_cache and value_cache must have the same shape and strides")
+    B, Hq, D = query.shape
+    Hkv = key_cache.size(2)
+    if key_cache.size(3) != D:
+        raise ValueError("head_dim of query and cache differ")
+    if query.dtype not in _DTYPES or key_cache.dtype != query.dtype:
+        raise ValueError("query and caches must share an fp16 or bf16 dtype")
+    _require_cuda(block_table, "block_table")
+    _require_cuda(cache_seqlens, "cache_seqlens")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.size(0) != B:
+        raise ValueError("block_table must be int32 [B, W]")
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    if cache_seqlens.dtype != torch.int32 or cache_seqlens.shape != (B,):
+        raise ValueError("cache_seqlens must be int32 [B]")
+    cache_seqlens = cache_seqlens.contiguous()
+    if out is None:
+        out = torch.empty_like(query, memory_format=torch.contiguous_format)
+    else:
+        _require_cuda(out, "out")
+        if out.shape != query.shape or out.dtype != query.dtype or out.stride(2) != 1 or out.stride(1) != D:
+            raise ValueError("out must match query's shape/dtype with contiguous heads")
+    if B == 0:
+        return out
+    W = block_table.size(1)
+    if W == 0:
+        raise ValueError("block_table has no columns")
+    if plan is None:
+        plan = DecodePlan(B, Hq, Hkv, D, query.device).plan(cache_seqlens, W)
+    elif (plan.batch, plan.num_q_heads, plan.num_kv_heads, plan.head_dim) != (B, Hq, Hkv, D) or plan.table_width != W:
+        raise ValueError("plan was built for a different batch / head layout / block-table width")
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    dev = query.device
+    with torch.cuda.device(dev):
+        st = lib.aeg_paged_attn_decode(out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
+                                       key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0),
+                                       key_cache.size(0), block_table.data_ptr(), block_table.stride(0),
+                                       cache_seqlens.data_ptr(), B, Hq, Hkv, D, scale, _DTYPES[query.dtype],
+                                       plan.workspace.data_ptr(), plan.workspace.numel(), _stream(dev))
+    check(st, "paged_attention_decode")
+    return out
+
+
+def paged_attention_decode(out: torch.Tensor, query: torch.Tensor, kv_cache: torch.Tensor, layer: int,
+                           block_tables: torch.Tensor, seq_lens: torch.Tensor, scale: float,
+                           plan: DecodePlan | None = None) -> None:
+    """Decode attention of ``layer`` over Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache, into ``out``."""
+    kc, vc = _layer_views(kv_cache, layer)
+    flash_attn_decode(query, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan)

@@ -1,0 +1,550 @@
+#!/usr/bin/env python
+"""Benchmark of the Aegaeon per-token serving hot path on B200.
+
+Default workload (``--config cfg2``): one Qwen2.5-7B decode step = 28 layers x (reshape_and_cache
+of one new token per sequence + paged decode attention), batch 64, lognormal contexts, a pool of
+16384 blocks (15 GB fp16). A step is captured once as a CUDA graph (plan + 56 kernels) and
+replayed; the KV read per step (1.6 GB) is far larger than the 126 MB L2, so no flush is needed.
+
+One JSON line on rank 0 (see the keys below). ``--impl reference`` times the CPU restatement of
+the reference's path (the oracle, all host threads) on the same workload.
+``--config cfg5`` measures the swap / copy_blocks path instead (GB/s).
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own cfg2 batch on its own pool
+(weak scaling, no data-path collective); the step time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    return p.parse_args()
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s earlier pool measurement)"
+
+
+def _ncu_traffic(kernel_key: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == kernel_key:
+                return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------------------------------
+# Clock sampling (nvidia-smi during the timed region)
+
+_CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.path = None
+        self.t0 = self.t1 = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ident, f"--query-gpu={_CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvidia-smi unavailable"}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "no samples"}
+        pmax = max(r["power"] for r in rows)
+        load = [r for r in rows if r["power"] >= 0.5 * pmax] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("swp", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": pmax}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU restatement timing (oracle): the reference arm and the cpu_baseline leg
+
+
+def _cpu_decode_setup(cfg, lay, seed=0):
+    """Compact host copy of the workload: only the blocks the batch uses, values N(0, std^2)."""
+    from aegaeon_b200.layout import BLOCK_SIZE
+    from oracle import oracle as orc
+
+    nb = (lay.seq_lens.astype(np.int64) + BLOCK_SIZE - 1) // BLOCK_SIZE
+    compact = np.zeros_like(lay.block_tables)
+    off = 0
+    for i, n in enumerate(nb):
+        compact[i, :n] = np.arange(off, off + n)
+        off += n
+    n_used = int(off)
+    g = torch.Generator().manual_seed(seed)
+    L, Hkv, D, Hq, B = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, cfg.num_q_heads, cfg.batch
+    # one layer's K/V blocks are enough: every layer call reads the same amount (layers differ only in
+    # their data), so the sample reuses this layer's values for each timed call.
+    kv = (torch.randn((n_used, 2, 16, Hkv, D), generator=g) * cfg.value_std).to(cfg.dtype)
+    kvb = kv.view(torch.int16).numpy().view(np.uint16)
+    q = (torch.randn((B, Hq, D), generator=g) * cfg.value_std).to(cfg.dtype).view(torch.int16).numpy().view(np.uint16)
+    knew = (torch.randn((B, Hkv, D), generator=g)).to(cfg.dtype).view(torch.int16).numpy().view(np.uint16)
+    slots = np.empty(B, np.int64)
+    pos = lay.seq_lens.astype(np.int64) - 1
+    slots[:] = compact[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16
+    dtype = orc.BF16 if cfg.dtype == torch.bfloat16 else orc.FP16
+    return dict(kvb=kvb, q=q, knew=knew, slots=slots, tables=compact, n_used=n_used, dtype=dtype)
+
+
+def _cpu_layer_call(cfg, lay, st, threads):
+    from oracle import oracle as orc
+
+    kvb = st["kvb"]
+    flat = kvb.reshape(-1)
+    blk = 2 * 16 * cfg.num_kv_heads * cfg.head_dim
+    half = 16 * cfg.num_kv_heads * cfg.head_dim
+    orc.c_reshape_and_cache(st["knew"], st["knew"], flat, flat[half:], blk, st["n_used"], st["slots"])
+    orc.c_paged_attention(st["q"], flat, flat[half:], blk, st["tables"], lay.seq_lens, cfg.num_kv_heads,
+                          1.0 / math.sqrt(cfg.head_dim), st["dtype"], threads)
+
+
+def cpu_decode_throughput(cfg, lay, budget_s: float, max_calls: int | None = None, warmup: int = 1):
+    """tokens/s of the CPU restatement: B / (mean layer-call time x L), plus the sample description."""
+    threads = _host_threads()
+    st = _cpu_decode_setup(cfg, lay)
+    for _ in range(warmup):
+        _cpu_layer_call(cfg, lay, st, threads)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        _cpu_layer_call(cfg, lay, st, threads)
+        times.append(time.perf_counter() - t0)
+        if max_calls is not None and len(times) >= max_calls:
+            break
+        if max_calls is None and time.perf_counter() - t_start >= budget_s:
+            break
+    per_layer = statistics.mean(times)
+    value = cfg.batch / (per_layer * cfg.num_layers)
+    sample = (f"{len(times)} layer calls (reshape_and_cache + decode attention over all {cfg.batch} sequences, "
+              f"sum ctx {lay.total_tokens}) timed, tokens/s = B / (mean call time x {cfg.num_layers} layers)")
+    return value, threads, sample, per_layer
+
+
+# ------------------------------------------------------------------------------------------
+# Our arm
+
+
+def _barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def _max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _per_launch_ms(fn_list, device, sleep_cycles=int(4e7)):
+    """Device durations of launches measured with CUDA events on the launching stream.
+
+    A sleep kernel is queued first so that the host enqueues every (event, launch, event) triple
+    before the device reaches them; launches then run back to back and each event pair brackets
+    exactly one kernel.
+    """
+    stream = torch.cuda.current_stream(device)
+    pairs = []
+    torch.cuda._sleep(sleep_cycles)
+    for fn in fn_list:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        pairs.append((e0, e1))
+    torch.cuda.synchronize(device)
+    return [a.elapsed_time(b) for a, b in pairs]
+
+
+def run_decode(args, world, rank, local):
+    from aegaeon_b200 import ops, synth
+    from aegaeon_b200.step import DecodeStep
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = synth.CONFIGS[args.config]
+    if cfg.name == "cfg3" and world > 1:
+        lay = synth.make_layout(cfg, rank, world)  # strong split of the batch across ranks
+        scaling = "strong"
+    else:
+        lay = synth.make_layout(cfg)
+        scaling = "weak"
+    B = len(lay.seq_lens)
+    L, Hq, Hkv, D = cfg.num_layers, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+    scale = synth.default_scale(cfg)
+
+    kv = torch.empty((lay.num_blocks, L, 2, 16, Hkv, D), dtype=cfg.dtype, device=device)
+    synth.fill_normal_(kv, cfg.value_std, cfg.seed + 1000 * rank)
+    step = DecodeStep(kv, Hq, B, lay.width, scale)
+    g = torch.Generator(device=device).manual_seed(cfg.seed + 17 + rank)
+    dev_inputs = dict(
+        q=(torch.randn(step.q.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+        k_new=(torch.randn(step.k_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+        v_new=(torch.randn(step.v_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+        slot_mapping=torch.as_tensor(synth.new_token_slots(lay), device=device),
+        block_tables=torch.as_tensor(lay.block_tables, device=device),
+        seq_lens=torch.as_tensor(lay.seq_lens, device=device),
+    )
+    host_inputs = {k: v.cpu().pin_memory() for k, v in dev_inputs.items()}
+    host_out = torch.empty(step.out.shape, dtype=step.out.dtype).pin_memory()
+    step.load_inputs(**dev_inputs)
+    step.capture()
+    torch.cuda.synchronize(device)
+
+    for _ in range(max(args.warmup, 3)):
+        step.replay()
+    torch.cuda.synchronize(device)
+
+    clocks = ClockSampler(device)
+    # Untimed pre-roll of ~1 s so that the clock samples cover the GPU under this load.
+    t_pre = time.perf_counter()
+    while time.perf_counter() - t_pre < 1.0:
+        for _ in range(50):
+            step.replay()
+        torch.cuda.synchronize(device)
+
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, device)
+    clock_info = clocks.stop()
+
+    # Per-launch durations of the dominant kernel (attention) and of the cache write.
+    n_prof = max(1, min(args.steps, 8))
+    attn_fns, write_fns = [], []
+    for _ in range(n_prof):
+        for layer in range(L):
+            attn_fns.append(lambda l=layer: ops.paged_attention_decode(step.out[l], step.q[l], kv, l, step.block_tables,
+                                                                       step.seq_lens, scale, plan=step.plan))
+            write_fns.append(lambda l=layer: ops.reshape_and_cache(step.k_new[l], step.v_new[l], kv, l,
+                                                                   step.slot_mapping))
+    attn_ms = []
+    for s in range(n_prof):
+        attn_ms += _per_launch_ms(attn_fns[s * L:(s + 1) * L], device)
+    write_ms = _per_launch_ms(write_fns[:L], device)
+    plan_ms = _per_launch_ms([lambda: step.plan.plan(step.seq_lens, lay.width)] * 4, device)
+
+    # End to end through the public step API with host buffers.
+    for _ in range(2):
+        step.run_from_host(host_inputs, host_out)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        step.run_from_host(host_inputs, host_out)
+    f1.record(stream)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world, device)
+
+    # Sanity: the timed outputs are finite (the work was done).
+    assert torch.isfinite(step.out.float()).all(), "non-finite attention output"
+
+    algo = synth.algorithmic_bytes_per_layer(cfg, lay)
+    ms_step = ms / args.steps
+    tokens_total = B * world
+    value = tokens_total / (ms_step / 1e3)
+    kv_step = algo["kv_read"] * L
+    attn_avg_ms = statistics.mean(attn_ms)
+    achieved = algo["attention"] / (attn_avg_ms / 1e3) / 1e9
+    peak, peak_src = _peaks()
+    traffic = _ncu_traffic(f"decode_attn_{cfg.name}")
+
+    line = {
+        "metric": "decode-attn tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": "fp16" if cfg.dtype == torch.float16 else "bf16",
+        "data": "synthetic: seeded contexts, block tables and N(0, std^2) K/V/q (no dataset on this path)",
+        "config": {
+            "workload": f"{cfg.name}: {cfg.model} decode step, {L} layers x (reshape_and_cache + paged decode "
+                        f"attention), one new token per sequence",
+            "batch_per_gpu": B, "layers": L, "q_heads": Hq, "kv_heads": Hkv, "head_dim": D, "block_size": 16,
+            "pool_blocks": lay.num_blocks, "sum_ctx": lay.total_tokens, "max_ctx": int(lay.seq_lens.max()),
+            "kv_bytes_per_step": kv_step, "accumulate": "fp32",
+            "l2": f"inputs larger than L2: {kv_step / 1e9:.2f} GB of K/V read per step vs 126 MB L2 (no flush)",
+            "parallelism": f"{world} GPU(s), one process each, own pool and batch, no collective",
+            "launch": "one CUDA graph per step (plan + per-layer cache write + attention, PDL)",
+        },
+        "kv_read_gbs": kv_step * world / (ms_step / 1e3) / 1e9,
+        "hbm_frac_step": (algo["attention"] + algo["reshape_and_cache"]) * L / (ms_step / 1e3) / 1e9 / peak,
+        "e2e": {
+            "value": tokens_total / (e2e_ms / args.steps / 1e3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": step.input_bytes(),
+            "d2h_bytes_per_step": step.output_bytes(),
+            "ms_per_step": e2e_ms / args.steps,
+            "path": "aegaeon_b200.step.DecodeStep.run_from_host: pinned host inputs -> H2D, graph replay, D2H out",
+        },
+        "gpu_launches": args.steps * step.launches_per_step,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "decode_attn_kernel",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_source": peak_src,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": algo["attention"],
+            "avg_launch_us": attn_avg_ms * 1e3,
+            "launches_timed": len(attn_ms),
+            "reshape_and_cache_avg_us": statistics.mean(write_ms) * 1e3,
+            "plan_avg_us": statistics.mean(plan_ms) * 1e3,
+        },
+        "clocks": clock_info,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        v, cores, sample, _ = cpu_decode_throughput(cfg, lay, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del step, kv
+
+
+def run_swap(args, world, rank, local):
+    """cfg5: swap out/in of 4096 scattered blocks and copy_blocks of 8192 pairs (GB/s)."""
+    from aegaeon_b200 import layout, ops, synth
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    c = synth.SWAP_CFG
+    shape = (c["device_blocks"],) + layout.kv_block_shape(c["num_layers"], c["num_kv_heads"], c["head_dim"])
+    kv = torch.empty(shape, dtype=c["dtype"], device=device)
+    synth.random_bits_(kv, c["seed"])
+    bb = layout.block_bytes(kv)
+    host = torch.empty((c["swap_blocks"],) + shape[1:], dtype=c["dtype"]).pin_memory()
+    g = torch.Generator().manual_seed(c["seed"])
+    out_ids = torch.randperm(c["device_blocks"], generator=g)[:c["swap_blocks"]].tolist()
+    host_ids = torch.randperm(c["swap_blocks"], generator=g).tolist()
+    in_ids = torch.randperm(c["device_blocks"], generator=g)[:c["swap_blocks"]].tolist()
+    p = torch.randperm(c["device_blocks"], generator=g)
+    src = p[:c["copy_pairs"]].to(device)
+    dst = p[c["copy_pairs"]:2 * c["copy_pairs"]].to(device)
+    d_out, d_host, d_in = (torch.as_tensor(x, device=device) for x in (out_ids, host_ids, in_ids))
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / reps
+
+    reps = max(1, min(args.steps, 5))
+    n = c["swap_blocks"]
+    res = {
+        "swap_out_dma_ms": timed(lambda: ops.swap(out_ids, host_ids, False, kv, host), reps),
+        "swap_in_dma_ms": timed(lambda: ops.swap(host_ids, in_ids, True, kv, host), reps),
+        "swap_out_sm_ms": timed(lambda: ops.swap_sm(d_out, d_host, False, kv, host), reps),
+        "swap_in_sm_ms": timed(lambda: ops.swap_sm(d_host, d_in, True, kv, host), reps),
+        "copy_blocks_ms": timed(lambda: ops.copy_blocks(src, dst, kv), max(reps, 10)),
+    }
+    # host-link reference: one contiguous pinned 1 GiB copy each way
+    big_h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    big_d = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    res["link_h2d_gbs"] = (1 << 30) / (timed(lambda: big_d.copy_(big_h, non_blocking=True), 5) / 1e3) / 1e9
+    res["link_d2h_gbs"] = (1 << 30) / (timed(lambda: big_h.copy_(big_d, non_blocking=True), 5) / 1e3) / 1e9
+    gbs = {k.replace("_ms", "_gbs"): (n * bb if "swap" in k else 2 * c["copy_pairs"] * bb) / (v / 1e3) / 1e9
+           for k, v in res.items() if k.endswith("_ms")}
+    best_swap = max(gbs["swap_out_dma_gbs"], gbs["swap_out_sm_gbs"])
+    peak, peak_src = _peaks()
+    line = {
+        "metric": "KV-block swap GB/s", "value": best_swap, "unit": "GB/s", "n_gpus": 1, "steps": reps,
+        "warmup": 2, "ms_per_step": min(res["swap_out_dma_ms"], res["swap_out_sm_ms"]), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u16", "data": "synthetic random 16-bit patterns",
+        "config": {"workload": "cfg5: 4096 scattered 917,504-byte blocks HBM -> pinned host (swap-out); "
+                               "back into fresh ids; copy_blocks 8192 pairs"},
+        "detail_ms": res, "detail_gbs": gbs,
+        "swap_frac_of_link": {"out": best_swap / res["link_d2h_gbs"],
+                              "in": max(gbs["swap_in_dma_gbs"], gbs["swap_in_sm_gbs"]) / res["link_h2d_gbs"]},
+        "roofline": {"bound": "hbm", "kernel": "block_copy_vec_kernel (copy_blocks)", "achieved": gbs["copy_blocks_gbs"],
+                     "peak": peak, "unit": "GB/s", "frac": gbs["copy_blocks_gbs"] / peak, "peak_source": peak_src,
+                     "traffic": _ncu_traffic("copy_blocks_cfg5")},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+# Reference arm: the CPU restatement of the reference's path on the host cores
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from aegaeon_b200 import synth
+
+    name = args.config if args.config != "cfg5" else "cfg2"
+    cfg = synth.CONFIGS[name]
+    lay = synth.make_layout(cfg)
+    # each step is one layer call of the full batch; cap the count so the run stays within minutes
+    budget_calls = args.steps
+    t_probe = time.perf_counter()
+    threads = _host_threads()
+    st = _cpu_decode_setup(cfg, lay)
+    _cpu_layer_call(cfg, lay, st, threads)
+    one = time.perf_counter() - t_probe
+    max_calls = max(1, min(budget_calls, int(150.0 / max(one, 1e-3))))
+    for _ in range(min(args.warmup, 3)):
+        _cpu_layer_call(cfg, lay, st, threads)
+    times = []
+    for _ in range(max_calls):
+        t0 = time.perf_counter()
+        _cpu_layer_call(cfg, lay, st, threads)
+        times.append(time.perf_counter() - t0)
+    per_layer = statistics.mean(times)
+    value = cfg.batch / (per_layer * cfg.num_layers)
+    sample = (f"{len(times)} of {args.steps} requested steps, each one layer call (reshape_and_cache + decode "
+              f"attention over all {cfg.batch} sequences, sum ctx {lay.total_tokens}); tokens/s = "
+              f"B / (mean call time x {cfg.num_layers} layers)")
+    line = {
+        "metric": "decode-attn tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": len(times),
+        "warmup": min(args.warmup, 3), "ms_per_step": per_layer * cfg.num_layers * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp64 (restatement)", "impl": "reference",
+        "data": "synthetic: seeded contexts, block tables and N(0, std^2) values",
+        "config": {"workload": f"{cfg.name}: {cfg.model} decode step, {cfg.num_layers} layers x (reshape_and_cache + "
+                               f"paged decode attention)", "batch_per_gpu": cfg.batch, "sum_ctx": lay.total_tokens},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference's attention and cache write live in un-vendored vLLM 0.5.1 with no CPU path; "
+                 "this arm runs the C restatement of the path (oracle/oracle.c) with all host threads"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = _args()
+    world, rank, local = _dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                             device_id=torch.device("cuda", local))
+    try:
+        if args.config == "cfg5":
+            if rank == 0:
+                run_swap(args, world, rank, local)
+        else:
+            run_decode(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,167 @@
+/*
+ * aegaeon_b200 — C ABI of the B200-native per-token serving path of Aegaeon.
+ *
+ * The library replaces four operations of the reference serving path:
+ *
+ *   aeg_swap               aegaeon/ops/swap.cu:25-60 (declared aegaeon/ops/ops.h:4-10,
+ *                          bound to Python at aegaeon/ops/ops.cpp:4-5 as `aegaeon.ops.swap`)
+ *   aeg_copy_blocks        vLLM 0.5.1 `_C_cache_ops.copy_blocks` (the API that the reference's
+ *                          GPU->GPU migration stubs at aegaeon/aegaeon/block_manager.py:876-950
+ *                          and aegaeon/aegaeon/worker.py:841-858 would call)
+ *   aeg_reshape_and_cache  vLLM 0.5.1 `_C_cache_ops.reshape_and_cache_flash`, reached per layer
+ *                          from the model forward at aegaeon/aegaeon/worker.py:517-523
+ *   aeg_decode_plan +      vLLM 0.5.1 FlashAttention backend decode call
+ *   aeg_paged_attn_decode  `flash_attn_with_kvcache(q, K_l, V_l, block_table, cache_seqlens, ...)`
+ *                          with the metadata built at aegaeon/aegaeon/worker.py:554-713
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are plain addresses; sizes are element or byte counts as named.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call is asynchronous on `stream` and returns an aeg_status; 0 is success.
+ *     On a non-zero status nothing was enqueued and aeg_last_error() (thread-local)
+ *     describes the problem.
+ *   - Host-side validation (shapes, alignment, id ranges of host id lists) happens before
+ *     any launch. Device-resident ids and slots that are out of range are skipped by the
+ *     kernels and reported through the device error word (aeg_read_device_errors).
+ *
+ * KV-cache geometry (Aegaeon's storage layout, aegaeon/aegaeon/worker.py:388-451 and
+ * aegaeon/aegaeon/config.py:256-271): kv_cache[num_blocks][L][2][16][Hkv][D], 16 tokens per
+ * block. Per layer l, the K view is kv_cache[:, l, 0] and the V view is kv_cache[:, l, 1]; both
+ * have a block stride of L*2*16*Hkv*D elements and a contiguous (16, Hkv, D) block interior.
+ * The attention and cache-write entry points take K and V base pointers plus that block
+ * stride, so vLLM's own (2, N, 16, Hkv, D) layout works as well.
+ */
+#ifndef AEGAEON_B200_H_
+#define AEGAEON_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AEG_API __attribute__((visibility("default")))
+#else
+#define AEG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  AEG_OK = 0,
+  AEG_ERR_INVALID_ARGUMENT = 1, /* shape, range, alignment or null-pointer problem */
+  AEG_ERR_CUDA = 2,             /* a CUDA runtime/driver call failed */
+  AEG_ERR_UNSUPPORTED = 3,      /* valid input this build does not handle (e.g. head_dim) */
+} aeg_status;
+
+typedef enum {
+  AEG_DTYPE_FP16 = 0,
+  AEG_DTYPE_BF16 = 1,
+} aeg_dtype;
+
+/* Device error bits (aeg_read_device_errors). */
+#define AEG_DEVERR_BLOCK_ID_RANGE 0x1u /* a block id outside [0, num_blocks) was skipped   */
+#define AEG_DEVERR_SLOT_RANGE 0x2u     /* a cache slot outside [0, num_blocks*16) skipped   */
+#define AEG_DEVERR_SEQ_LEN_RANGE 0x4u  /* seq_len < 0 or > 16 * block-table width, clamped  */
+#define AEG_DEVERR_WAIT_TIMEOUT 0x8u   /* a bounded pipeline wait gave up (output invalid)   */
+#define AEG_DEVERR_PLAN_MISMATCH 0x10u /* the workspace plan does not fit this call; skipped  */
+
+/* Library version (major*10000 + minor*100 + patch). */
+AEG_API int aeg_version(void);
+
+/* Message for the last non-zero status returned on the calling thread. */
+AEG_API const char* aeg_last_error(void);
+
+/* Reads and clears the sticky device error word of the current device (synchronises
+ * `stream`). *flags receives an OR of AEG_DEVERR_* bits raised since the last read. */
+AEG_API int aeg_read_device_errors(void* stream, uint32_t* flags);
+
+/* ---------------------------------------------------------------------------------------
+ * a1. swap — replaces aegaeon/ops/swap.cu:25-60 (`ops.swap(source_block_ids,
+ * target_block_ids, is_swap_in, kv_cache, kv_swap)`).
+ *
+ * Copies whole blocks of `block_bytes` between the device pool `dev_pool` (n_dev_blocks
+ * blocks) and the host pool `host_pool` (n_host_blocks blocks): for i < n,
+ *   is_swap_in != 0: dev_pool[dst_ids[i]]  <- host_pool[src_ids[i]]   (H2D)
+ *   is_swap_in == 0: host_pool[dst_ids[i]] <- dev_pool[src_ids[i]]    (D2H)
+ * `src_ids`/`dst_ids` are HOST arrays (the reference passes std::vector<int64_t>). Every id is
+ * range-checked on the host before anything is enqueued (the reference checks nothing).
+ * Consecutive ids that are adjacent on both sides are merged into one transfer. The host pool
+ * should be page-locked (cudaHostRegister / cudaHostAlloc) for the copy to be asynchronous.
+ */
+AEG_API int aeg_swap(void* dev_pool, void* host_pool, size_t block_bytes, int64_t n_dev_blocks,
+             int64_t n_host_blocks, const int64_t* src_ids, const int64_t* dst_ids, int64_t n,
+             int is_swap_in, void* stream);
+
+/* a1 (SM-driven variant). Same data movement as aeg_swap, done by a kernel that reads and
+ * writes the page-locked host pool through its mapped device address, so any number of
+ * scattered blocks costs one launch. `d_src_ids`/`d_dst_ids` are DEVICE int64 arrays; ids out
+ * of range are skipped and raise AEG_DEVERR_BLOCK_ID_RANGE. `host_pool` must be page-locked
+ * and mapped (cudaHostGetDevicePointer must succeed for it), else AEG_ERR_INVALID_ARGUMENT. */
+AEG_API int aeg_swap_sm(void* dev_pool, void* host_pool, size_t block_bytes, int64_t n_dev_blocks,
+                int64_t n_host_blocks, const int64_t* d_src_ids, const int64_t* d_dst_ids,
+                int64_t n, int is_swap_in, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * a8. copy_blocks — the vLLM 0.5.1 `copy_blocks` operation on Aegaeon's whole-block layout.
+ * For i < n: pool[dst_ids[i]] <- pool[src_ids[i]] (block_bytes each). `d_src_ids`/`d_dst_ids`
+ * are DEVICE int64 arrays. Pairs are applied concurrently: a block that is both a source and a
+ * destination within one call gives an unspecified result (as in vLLM). Out-of-range ids are
+ * skipped and raise AEG_DEVERR_BLOCK_ID_RANGE.
+ */
+AEG_API int aeg_copy_blocks(void* pool, size_t block_bytes, int64_t num_blocks, const int64_t* d_src_ids,
+                    const int64_t* d_dst_ids, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * a6. reshape_and_cache — replaces vLLM 0.5.1 `reshape_and_cache_flash(key, value, key_cache,
+ * value_cache, slot_mapping, "auto")` as called per layer inside the model forward
+ * (aegaeon/aegaeon/worker.py:517-523, slot mapping built at worker.py:628-633).
+ *
+ * For t < T with s = slot_mapping[t] >= 0:
+ *   k_cache[(s / 16) * block_stride + (s % 16) * Hkv * D + h * D + d] = key[t * key_stride + h * D + d]
+ * and the same for value/v_cache. Slots < 0 are skipped (padding), as in vLLM. Slots
+ * >= num_blocks * 16 are skipped and raise AEG_DEVERR_SLOT_RANGE. Elements are 2 bytes
+ * (fp16 or bf16; the copy is bit-exact and dtype-blind). `key_stride`/`value_stride` are the
+ * token strides of key/value in elements; `block_stride` is in elements.
+ */
+AEG_API int aeg_reshape_and_cache(const void* key, const void* value, int64_t key_stride,
+                          int64_t value_stride, void* k_cache, void* v_cache,
+                          int64_t block_stride, int64_t num_blocks,
+                          const int64_t* slot_mapping, int64_t T, int Hkv, int D, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * a7. Paged decode attention — replaces the decode half of the vLLM 0.5.1 FlashAttention
+ * backend: flash_attn_with_kvcache(q[:, None], K_l, V_l, block_table=block_tables,
+ * cache_seqlens=seq_lens, softmax_scale=scale, causal=True) with one query token per
+ * sequence. For b < B, h < Hq, with G = Hq / Hkv and n = seq_lens[b]:
+ *   out[b, h] = sum_{j<n} softmax_j(scale * q[b,h] . K[blk(b,j), j%16, h/G]) * V[blk(b,j), j%16, h/G]
+ *   blk(b, j) = block_tables[b * table_stride + j / 16]
+ * computed in fp32 and rounded to the storage dtype. seq_len 0 gives a zero row.
+ *
+ * A decode step runs aeg_decode_plan once (it depends only on seq_lens, like the per-step
+ * attention metadata at worker.py:694-711) and then aeg_paged_attn_decode once per layer
+ * with the same workspace. The workspace is caller-owned device memory of at least
+ * aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by one stream at
+ * a time. The plan splits every (sequence, kv-head group) into block ranges of balanced size
+ * so that all SMs stream the same number of KV bytes; split results are merged inside the
+ * attention launch by the last CTA to finish each sequence.
+ *
+ * Supported: D = 128; Hq % Hkv == 0; Hq / Hkv <= 16; fp16 or bf16; 16-byte aligned K/V
+ * bases and block stride; q/out token strides that are multiples of 8 elements.
+ */
+AEG_API size_t aeg_decode_workspace_size(int B, int Hq, int Hkv, int D);
+
+AEG_API int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* seq_lens, int B,
+                    int Hq, int Hkv, int D, int table_stride, void* stream);
+
+AEG_API int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                          const void* k_cache, const void* v_cache, int64_t block_stride,
+                          int64_t num_blocks, const int32_t* block_tables, int table_stride,
+                          const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale,
+                          int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AEGAEON_B200_H_ */

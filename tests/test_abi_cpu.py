@@ -1,0 +1,131 @@
+"""The C-ABI library loads, exports every declared symbol, and validates on the host (no GPU)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from aegaeon_b200 import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "aegaeon_b200.h")
+
+
+def _declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"AEG_API\s+[\w\s\*]+?\b(aeg_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_path():
+    syms = _declared_symbols()
+    for name in ("aeg_swap", "aeg_swap_sm", "aeg_copy_blocks", "aeg_reshape_and_cache", "aeg_decode_plan",
+                 "aeg_paged_attn_decode", "aeg_decode_workspace_size", "aeg_last_error", "aeg_read_device_errors"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = [s for s in _declared_symbols() if s not in exported]
+    assert not missing, missing
+    # the Python binding covers the same set
+    assert set(_native.SIGNATURES) == set(_declared_symbols())
+    # nothing else leaks out of the library under the aeg_ prefix
+    assert {s for s in exported if s.startswith("aeg_")} == set(_declared_symbols())
+
+
+def test_version_and_workspace_size():
+    lib = _native.lib
+    assert lib.aeg_version() >= 100
+    ws = lib.aeg_decode_workspace_size(64, 28, 4, 128)
+    assert ws > 0 and ws % 256 == 0
+    assert lib.aeg_decode_workspace_size(64, 28, 5, 128) == 0  # Hq not a multiple of Hkv
+    assert lib.aeg_decode_workspace_size(256, 32, 4, 128) > lib.aeg_decode_workspace_size(64, 32, 4, 128)
+
+
+def _fake(n=1 << 20):
+    buf = (ctypes.c_uint8 * n)()
+    return ctypes.addressof(buf), buf
+
+
+def test_swap_rejects_out_of_range_ids_before_any_copy():
+    lib = _native.lib
+    dev, _k1 = _fake()
+    host, _k2 = _fake()
+    src = np.array([0, 5], np.int64)
+    dst = np.array([1, 2], np.int64)
+    st = lib.aeg_swap(dev, host, 64, 4, 4, src.ctypes.data, dst.ctypes.data, 2, 0, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT
+    assert "source block id 5" in _native.last_error()
+    st = lib.aeg_swap(dev, host, 64, 8, 2, src.ctypes.data, dst.ctypes.data, 2, 0, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT and "target block id 2" in _native.last_error()
+    neg = np.array([-1], np.int64)
+    st = lib.aeg_swap(dev, host, 64, 8, 8, neg.ctypes.data, dst.ctypes.data, 1, 1, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT
+    assert lib.aeg_swap(dev, host, 64, 8, 8, src.ctypes.data, dst.ctypes.data, -1, 1, None) == 1
+    assert lib.aeg_swap(dev, host, 64, 8, 8, src.ctypes.data, dst.ctypes.data, 0, 1, None) == 0  # empty: no-op
+
+
+def test_decode_validation_on_host():
+    lib = _native.lib
+    p, _k = _fake()
+    # unsupported head dim
+    st = lib.aeg_decode_plan(p, 1 << 30, p, 4, 28, 4, 64, 16, None)
+    assert st == _native.AEG_ERR_UNSUPPORTED and "head_dim" in _native.last_error()
+    # GQA group too large
+    st = lib.aeg_decode_plan(p, 1 << 30, p, 4, 68, 4, 128, 16, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT
+    # misaligned workspace
+    st = lib.aeg_decode_plan(p + 1, 1 << 30, p, 4, 28, 4, 128, 16, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT and "aligned" in _native.last_error()
+    # workspace too small
+    need = lib.aeg_decode_workspace_size(4, 28, 4, 128)
+    aligned = (p + 255) // 256 * 256
+    st = lib.aeg_decode_plan(aligned, need - 1, p, 4, 28, 4, 128, 16, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT and "need" in _native.last_error()
+    # attention: bad dtype, misaligned cache base
+    args = dict(out=p, q=p, k=p, v=p)
+    st = lib.aeg_paged_attn_decode(p, 28 * 128, p, 28 * 128, p, p, 28 * 2 * 16 * 4 * 128, 64, p, 16, p, 4, 28, 4,
+                                   128, 0.1, 7, aligned, need, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT and "dtype" in _native.last_error()
+    st = lib.aeg_paged_attn_decode(p, 28 * 128, p, 28 * 128, p + 2, p, 28 * 2 * 16 * 4 * 128, 64, p, 16, p, 4, 28, 4,
+                                   128, 0.1, 0, aligned, need, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT and "16-byte" in _native.last_error()
+    del args
+
+
+def test_reshape_and_cache_validation_on_host():
+    lib = _native.lib
+    p, _k = _fake()
+    # token stride smaller than a row
+    st = lib.aeg_reshape_and_cache(p, p, 100, 512, p, p, 16 * 512, 8, p, 4, 4, 128, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT
+    # block stride smaller than 16 rows
+    st = lib.aeg_reshape_and_cache(p, p, 512, 512, p, p, 512, 8, p, 4, 4, 128, None)
+    assert st == _native.AEG_ERR_INVALID_ARGUMENT
+    assert lib.aeg_reshape_and_cache(p, p, 512, 512, p, p, 16 * 512, 8, p, 0, 4, 128, None) == 0  # T = 0
+
+
+def test_copy_blocks_validation_on_host():
+    lib = _native.lib
+    p, _k = _fake()
+    assert lib.aeg_copy_blocks(p, 64, 8, p, p, -3, None) == _native.AEG_ERR_INVALID_ARGUMENT
+    assert lib.aeg_copy_blocks(p, 64, 8, p, p, 0, None) == 0
+    assert lib.aeg_copy_blocks(p, 64, 8, p + 1, p, 2, None) == _native.AEG_ERR_INVALID_ARGUMENT
+
+
+def test_ops_module_imports_and_fails_loudly_without_cuda():
+    import torch
+
+    from aegaeon_b200 import ops
+
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only check")
+    kv = torch.zeros((4, 1, 2, 16, 4, 128), dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.copy_blocks([0], [1], kv)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.swap([0], [1], False, kv, torch.zeros_like(kv))
