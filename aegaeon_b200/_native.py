@@ -41,10 +41,13 @@ SIGNATURES = {
     "aeg_reshape_and_cache": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                      _c_void_p, _i64, _i32, _i32, _c_void_p]),
     "aeg_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
-    "aeg_decode_plan": (_i32, [_c_void_p, _sz, _c_void_p, _i32, _i32, _i32, _i32, _i32, _c_void_p]),
+    "aeg_decode_plan": (_i32, [_c_void_p, _sz, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p]),
     "aeg_paged_attn_decode": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                      _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, ctypes.c_float, _i32,
                                      _c_void_p, _sz, _c_void_p]),
+    "aeg_decode_layer": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p,
+                                _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,
+                                ctypes.c_float, _i32, _c_void_p, _sz, _c_void_p]),
 }
 
 

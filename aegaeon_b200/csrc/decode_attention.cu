@@ -7,24 +7,31 @@
 // KV head h / (Hq / Hkv).
 //
 // Design (memory-bound: every K/V byte is read exactly once per layer call):
-//   * Work unit = (sequence b, group of HG KV heads, range of 16-token blocks). A plan kernel,
-//     run once per decode step, splits every (b, group) into ranges of near-equal length so
-//     that all CTAs stream the same number of bytes.
-//   * Persistent CTAs: HG consumer warps (one per KV head of the group) + 1 producer warp.
-//     The producer streams each block's K and V boxes (16 tokens x HG heads x 128 dims) into a
-//     STAGES-deep shared-memory ring with 5-D bulk-tensor TMA loads (128-byte swizzle,
-//     evict-first L2 policy), completing on mbarriers. For Aegaeon's layout a (block, layer)
-//     K or V box is one contiguous 16 KiB span at Hkv = 4.
-//   * Consumers compute S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query heads of the
-//     GQA group; K fragments by ldmatrix from the swizzled tile), fp32 online softmax in the
-//     exp2 domain with quad shuffles, transpose P in registers with movmatrix, then
-//     O^T += V^T P^T (V fragments by ldmatrix.trans). Tensor cores carry the G query heads
-//     that share one K/V tile, so the CUDA cores only do the softmax.
-//   * A unit that covers a whole sequence writes the output row directly. Split units write
-//     fp32 partials (unnormalised O, running max, running sum); the last CTA of a (b, group)
-//     to finish (atomic ticket, no spinning) merges them and resets its counter.
+//   * Work unit = (sequence b, KV head h, range of 16-token blocks). A plan kernel, run once
+//     per decode step, cuts every (b, h) into ranges of near-equal length (at most kMaxSplits)
+//     and orders the units longest first. A unit record also carries the sequence length and
+//     the unit's first three block ids.
+//   * Every warp is an independent worker (kWarps per CTA, one CTA per SM). Its first unit is
+//     its warp index, later ones come from an atomic work counter (dynamic load balance; the
+//     last warp to exit resets it for the next launch). It streams each (block, head) K and V
+//     tile (16 tokens x 128 dims, 4 KiB each) into its own kStages-deep shared-memory ring with
+//     5-D bulk-tensor TMA loads (128-byte swizzle, evict-first L2 policy) completing on
+//     mbarriers. The next unit's record, block-table chunk and query rows (1-D bulk copy) are
+//     prefetched one phase per processed block, and the ring keeps streaming across unit
+//     boundaries. No CTA-wide barrier is taken after set-up.
+//   * Per block the warp computes S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query
+//     heads of the GQA group; K fragments by ldmatrix from the swizzled tile), an fp32 online
+//     softmax in the exp2 domain with quad shuffles, transposes P in registers with movmatrix
+//     and accumulates O^T += V^T P^T (V fragments by ldmatrix.trans). For bf16, P enters as a
+//     bf16 value plus its bf16 rounding residue (two MMAs) so that P V keeps ~16 mantissa bits.
+//   * A unit covering a whole (b, h) writes the output rows; a split unit writes an fp32
+//     partial (O scaled by 2^-max, max, sum). A combine kernel, launched right after with
+//     programmatic dependent launch, merges the partials of every split (b, h): one warp per
+//     (b, h, query head), all of its loads in one or two round trips.
+//   * Fused form (aeg_decode_layer): the warp that reads a sequence's newest block writes the
+//     new token's K/V row of its head into the cache and patches it into the tile.
 //   * Every mbarrier wait is bounded (2 s); a timeout raises AEG_DEVERR_WAIT_TIMEOUT and the
-//     kernel drains instead of hanging.
+//     warp drains instead of hanging.
 #include "aeg_common.cuh"
 
 #include <cuda.h>
@@ -33,6 +40,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 namespace aeg {
 namespace {
@@ -40,51 +48,61 @@ namespace {
 __device__ unsigned int g_deverr_attn = 0;
 
 constexpr int kHeadDim = 128;
-constexpr int kHalves = kHeadDim / 64;   // 128-byte rows per (token, head)
+constexpr int kHalves = kHeadDim / 64;  // 128-byte rows per (token, head)
 constexpr int kBlockTokens = 16;
-constexpr int kMaxTargetUnits = 4096;    // upper bound on the plan's balanced unit count
-constexpr int kPlanThreads = 1024;
+constexpr int kMaxTargetUnits = 8192;   // upper bound on the plan's balanced unit count
+constexpr int kMaxSplits = 64;          // splits of one (sequence, KV head) at most
+constexpr int kMinChunk = 4;            // blocks per unit at least (unless the sequence is shorter)
+constexpr int kPlanThreads = 256;
+constexpr int kPlanBins = 1024;         // size classes of the longest-first unit order
+constexpr int kPlanCachedSeqs = 4096;   // sequences whose block counts the plan keeps in smem
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+constexpr int kWarps = 8;               // independent workers per CTA (one CTA per SM)
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 3;              // per-warp ring depth
+constexpr int kBoxBytes = kHalves * kBlockTokens * 128;  // one (block, head) K or V tile: 4 KiB
+constexpr int kStageBytes = 2 * kBoxBytes;
+
+// Header words of the workspace.
+constexpr int kHdrUnits = 0, kHdrChunk = 1, kHdrPairs = 2, kHdrSplitPairs = 3, kHdrWork = 8, kHdrExit = 9;
 
 // ---------------------------------------------------------------------------------------
 // Workspace layout (all offsets 256-byte aligned):
-//   header   : int32[64]  {num_units, chunk_blocks, num_pairs, ...}
-//   counters : int32[P]   per (sequence, KV-head group) split tickets, zeroed by the plan
-//   units    : int4[max_units]  {pair, j0, j1, (split << 16) | nsplit}
-//   part_ml  : float2[max_units * HG * G]          (running max in log2 units, running sum)
-//   part_o   : float [max_units * HG * G * D]      unnormalised partial outputs
+//   header      : int32[64]  {num_units, chunk, num_pairs, num_split_pairs, .., work, exit}
+//   split_pairs : int4[P]    {pair, first unit, nsplit, 0} of every split (sequence, head)
+//   units       : int4[2 * max_units]  {pair, j0, j1, (split << 16) | nsplit},
+//                                      {seq_len, block id of items 0, 1, 2}
+//   part_ml     : float2[max_units * G]        (max in log2 units, sum) per query head
+//   part_o      : float [max_units * G * D]    partial outputs, scaled by 2^-max
 struct WsLayout {
-  size_t counters, units, part_ml, part_o, total;
+  size_t split_pairs, units, part_ml, part_o, total;
   int max_units;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-inline int pick_hg(int Hkv) { return (Hkv % 4 == 0) ? 4 : (Hkv % 2 == 0 ? 2 : 1); }
-
 WsLayout ws_layout(int B, int Hq, int Hkv, int D) {
   WsLayout w{};
-  const int hg = pick_hg(Hkv);
-  const int ng = Hkv / hg;
   const int G = Hq / Hkv;
-  const int64_t P = int64_t(B) * ng;
+  const int64_t P = int64_t(B) * Hkv;
   w.max_units = static_cast<int>(kMaxTargetUnits + P);
   size_t off = 256;
-  w.counters = off;
-  off = align256(off + sizeof(int) * P);
+  w.split_pairs = off;
+  off = align256(off + sizeof(int4) * P);
   w.units = off;
-  off = align256(off + sizeof(int4) * size_t(w.max_units));
+  off = align256(off + 2 * sizeof(int4) * size_t(w.max_units));
   w.part_ml = off;
-  off = align256(off + sizeof(float2) * size_t(w.max_units) * hg * G);
+  off = align256(off + sizeof(float2) * size_t(w.max_units) * G);
   w.part_o = off;
-  off = align256(off + sizeof(float) * size_t(w.max_units) * hg * G * D);
+  off = align256(off + sizeof(float) * size_t(w.max_units) * G * D);
   w.total = off;
   return w;
 }
 
 struct WsPtrs {
   int* header;
-  int* counters;
+  int4* split_pairs;
   int4* units;
   float2* part_ml;
   float* part_o;
@@ -92,79 +110,167 @@ struct WsPtrs {
 
 inline WsPtrs ws_ptrs(void* ws, const WsLayout& L) {
   char* b = static_cast<char*>(ws);
-  return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int*>(b + L.counters), reinterpret_cast<int4*>(b + L.units),
-                reinterpret_cast<float2*>(b + L.part_ml), reinterpret_cast<float*>(b + L.part_o)};
+  return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int4*>(b + L.split_pairs),
+                reinterpret_cast<int4*>(b + L.units), reinterpret_cast<float2*>(b + L.part_ml),
+                reinterpret_cast<float*>(b + L.part_o)};
 }
 
 // ---------------------------------------------------------------------------------------
-// Plan kernel (one CTA): chunk size, per-(b, group) split counts, unit list.
+// Plan kernel (one CTA): chunk size, split counts, unit list, split-pair list.
 
-__device__ __forceinline__ int clamp_len(int n, int cap) {
+__device__ __forceinline__ int seq_blocks(const int* seq_lens, int b, int cap, bool report) {
+  int n = seq_lens[b];
   if (n < 0 || n > cap) {
-    atomicOr(&g_deverr_attn, AEG_DEVERR_SEQ_LEN_RANGE);
-    return n < 0 ? 0 : cap;
+    if (report) atomicOr(&g_deverr_attn, AEG_DEVERR_SEQ_LEN_RANGE);
+    n = n < 0 ? 0 : cap;
   }
-  return n;
+  return (n + kBlockTokens - 1) / kBlockTokens;
 }
 
+__device__ __forceinline__ int splits_for(int nb, int chunk) {
+  int ns = (nb + chunk - 1) / chunk;
+  ns = ns < 1 ? 1 : ns;
+  return ns > kMaxSplits ? kMaxSplits : ns;
+}
+
+__device__ __forceinline__ int size_bin(int nb, int chunk) {
+  if (chunk < kPlanBins) return nb;
+  const long long b = static_cast<long long>(nb) * (kPlanBins - 1) / chunk;
+  return static_cast<int>(b);
+}
+
+// Block-wide exclusive scan of one int per thread; also returns the total.
+__device__ __forceinline__ int block_excl_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  __syncthreads();
+  if (lane == 31) s_warp[wid] = incl;
+  __syncthreads();
+  int off = 0;
+  total = 0;
+  for (int i = 0; i < kPlanThreads / 32; ++i) {
+    if (i < wid) off += s_warp[i];
+    total += s_warp[i];
+  }
+  return off + incl - v;
+}
+
+// Unit order, longest first: all units of split (sequence, head) pairs (each about `chunk`
+// blocks) in pair order, then the unsplit pairs by decreasing block count. Workers take units
+// in this order, so the tail of a launch is made of the smallest ones.
 __global__ void __launch_bounds__(kPlanThreads)
-decode_plan_kernel(const int* __restrict__ seq_lens, int B, int NG, int table_stride, int target_units,
-                   WsPtrs ws) {
+decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tables, int B, int Hkv,
+                   int table_stride, int target_units, WsPtrs ws) {
   __shared__ long long s_red[kPlanThreads / 32];
-  __shared__ int s_scan[kPlanThreads];
-  const int tid = threadIdx.x;
-  const int P = B * NG;
+  __shared__ int s_warp[kPlanThreads / 32];
+  __shared__ int s_hist[kPlanBins];
+  __shared__ int s_cursor[kPlanBins];
+  __shared__ int s_nb[kPlanCachedSeqs];  // blocks per sequence (first kPlanCachedSeqs sequences)
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int P = B * Hkv;
   const int cap = table_stride * kBlockTokens;
 
-  // Pass 1: total blocks over all (b, group) pairs.
-  long long local = 0;
-  for (int p = tid; p < P; p += kPlanThreads) {
-    const int n = clamp_len(seq_lens[p / NG], cap);
-    local += (n + kBlockTokens - 1) / kBlockTokens;
-  }
-  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-  if ((tid & 31) == 0) s_red[tid >> 5] = local;
-  __syncthreads();
-  if (tid < 32) {
-    long long v = s_red[tid];
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (tid == 0) s_red[0] = v;
-  }
-  __syncthreads();
-  const long long total = s_red[0];
-  const int chunk = static_cast<int>(max(1LL, (total + target_units - 1) / target_units));
+  for (int i = tid; i < kPlanBins; i += kPlanThreads) s_hist[i] = 0;
 
-  // Pass 2: each thread owns a contiguous range of pairs; exclusive scan of split counts.
+  // Pass 1: total (block, head) items -> chunk.
+  long long local = 0;
+  for (int b = tid; b < B; b += kPlanThreads) {
+    const int nb = seq_blocks(seq_lens, b, cap, true);
+    if (b < kPlanCachedSeqs) s_nb[b] = nb;
+    local += nb;
+  }
+  auto blocks_of = [&](int b) { return b < kPlanCachedSeqs ? s_nb[b] : seq_blocks(seq_lens, b, cap, false); };
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if (lane == 0) s_red[wid] = local;
+  __syncthreads();
+  long long total = 0;
+  for (int i = 0; i < kPlanThreads / 32; ++i) total += s_red[i];
+  total *= Hkv;
+  int chunk = static_cast<int>((total + target_units - 1) / target_units);
+  chunk = chunk < kMinChunk ? kMinChunk : chunk;
+
+  // Pass 2: split units and split pairs counted over contiguous pair ranges; unsplit pairs binned.
   const int per = (P + kPlanThreads - 1) / kPlanThreads;
   const int p0 = min(P, tid * per), p1 = min(P, p0 + per);
-  int cnt = 0;
+  int cnt_units = 0, cnt_pairs = 0;
   for (int p = p0; p < p1; ++p) {
-    const int nb = (min(max(seq_lens[p / NG], 0), cap) + kBlockTokens - 1) / kBlockTokens;
-    cnt += max(1, (nb + chunk - 1) / chunk);
-  }
-  s_scan[tid] = cnt;
-  __syncthreads();
-  for (int o = 1; o < kPlanThreads; o <<= 1) {
-    const int v = tid >= o ? s_scan[tid - o] : 0;
-    __syncthreads();
-    s_scan[tid] += v;
-    __syncthreads();
-  }
-  int u = s_scan[tid] - cnt;
-  for (int p = p0; p < p1; ++p) {
-    const int nb = (min(max(seq_lens[p / NG], 0), cap) + kBlockTokens - 1) / kBlockTokens;
-    const int ns = max(1, (nb + chunk - 1) / chunk);
-    for (int s = 0; s < ns; ++s) {
-      const int j0 = static_cast<int>((static_cast<long long>(s) * nb) / ns);
-      const int j1 = static_cast<int>((static_cast<long long>(s + 1) * nb) / ns);
-      ws.units[u++] = make_int4(p, j0, j1, (s << 16) | ns);
+    const int nb = blocks_of(p / Hkv);
+    const int ns = splits_for(nb, chunk);
+    if (ns > 1) {
+      cnt_units += ns;
+      ++cnt_pairs;
+    } else {
+      atomicAdd(&s_hist[size_bin(nb, chunk)], 1);
     }
-    ws.counters[p] = 0;
   }
-  if (tid == kPlanThreads - 1) {
-    ws.header[0] = s_scan[kPlanThreads - 1];
-    ws.header[1] = chunk;
-    ws.header[2] = P;
+  int n_split_units = 0, n_split_pairs = 0;
+  int u = block_excl_scan(cnt_units, s_warp, n_split_units);
+  int sp = block_excl_scan(cnt_pairs, s_warp, n_split_pairs);
+
+  // Descending-size offsets of the bins: thread t owns bins [4t, 4t + 4); the offset of its
+  // bins is the number of unsplit units in all higher bins (a reversed block scan).
+  static_assert(kPlanBins == 4 * kPlanThreads, "four bins per plan thread");
+  int loc[4], own = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    loc[i] = s_hist[4 * tid + i];
+    own += loc[i];
+  }
+  __syncthreads();
+  s_cursor[kPlanThreads - 1 - tid] = own;  // reversed order (scratch use of s_cursor)
+  __syncthreads();
+  int dummy = 0;
+  const int rexcl = block_excl_scan(s_cursor[tid], s_warp, dummy);
+  __syncthreads();
+  s_cursor[kPlanBins - 1 - tid] = rexcl;  // units owned by threads above (kPlanThreads - 1 - tid)
+  __syncthreads();
+  const int higher = s_cursor[kPlanBins - 1 - (kPlanThreads - 1 - tid)];
+  __syncthreads();
+  int run = n_split_units + higher;
+#pragma unroll
+  for (int i = 3; i >= 0; --i) {
+    s_cursor[4 * tid + i] = run;
+    run += loc[i];
+  }
+  if (tid == 0) {
+    ws.header[kHdrUnits] = run;  // thread 0 owns the lowest bins: its running end is the total
+    ws.header[kHdrChunk] = chunk;
+    ws.header[kHdrPairs] = P;
+    ws.header[kHdrSplitPairs] = n_split_pairs;
+    ws.header[kHdrWork] = 0;
+    ws.header[kHdrExit] = 0;
+  }
+  __syncthreads();
+
+  // Pass 3: write the units and the split-pair list. A unit record also carries the sequence
+  // length and its first three block ids, so that a worker can request its first tiles after
+  // one load.
+  auto put = [&](int idx, int p, int j0, int j1, int sw) {
+    const int b = p / Hkv;
+    const int* tb = tables + static_cast<int64_t>(b) * table_stride + j0;
+    const int n = j1 - j0;
+    const int n_ctx = min(max(seq_lens[b], 0), cap);
+    ws.units[2 * idx] = make_int4(p, j0, j1, sw);
+    ws.units[2 * idx + 1] = make_int4(n_ctx, n > 0 ? tb[0] : 0, n > 1 ? tb[1] : 0, n > 2 ? tb[2] : 0);
+  };
+  for (int p = p0; p < p1; ++p) {
+    const int nb = blocks_of(p / Hkv);
+    const int ns = splits_for(nb, chunk);
+    if (ns > 1) {
+      ws.split_pairs[sp++] = make_int4(p, u, ns, 0);
+      for (int s = 0; s < ns; ++s) {
+        const int j0 = static_cast<int>((static_cast<long long>(s) * nb) / ns);
+        const int j1 = static_cast<int>((static_cast<long long>(s + 1) * nb) / ns);
+        put(u++, p, j0, j1, (s << 16) | ns);
+      }
+    } else {
+      const int pos = atomicAdd(&s_cursor[size_bin(nb, chunk)], 1);
+      put(pos, p, 0, nb, 1);
+    }
   }
 }
 
@@ -180,21 +286,33 @@ struct AttnParams {
   int table_stride;
   const int* seq_lens;
   int G;
-  int NG;
-  int num_pairs;   // B * NG
-  int max_units;   // capacity of the workspace unit list
+  int Hkv;
+  int num_pairs;  // B * Hkv
+  int max_units;  // capacity of the workspace unit list
   int64_t num_blocks;
   float scale_log2;
+  int q_bulk;  // query rows are 16-byte aligned: stage them with bulk copies
+  // Fused cache write (decode_layer): the new token of sequence b (position seq_len - 1) is
+  // written into the cache and patched into the tile that holds it.
+  int fuse_write;
+  const void* k_new;
+  const void* v_new;
+  int64_t k_new_stride;  // token strides of k_new / v_new (elements)
+  int64_t v_new_stride;
+  void* k_cache;
+  void* v_cache;
+  int64_t block_stride;  // elements
   WsPtrs ws;
 };
 
 // A unit read from the workspace is used only if it is consistent with this call's shape; a
 // workspace that was not planned for this call (or not planned at all) is skipped and reported
 // instead of steering loads out of bounds.
-__device__ __forceinline__ bool unit_ok(const int4& un, int u, const AttnParams& p) {
+__device__ __forceinline__ bool unit_ok(const int4& un, const int4& un1, int u, const AttnParams& p) {
   const int split = un.w >> 16, nsplit = un.w & 0xffff;
   return un.x >= 0 && un.x < p.num_pairs && un.y >= 0 && un.y <= un.z && un.z <= p.table_stride && nsplit >= 1 &&
-         split < nsplit && u - split >= 0 && u - split + nsplit <= p.max_units;
+         nsplit <= kMaxSplits && split < nsplit && u - split >= 0 && u - split + nsplit <= p.max_units &&
+         un1.x >= 0 && un1.x <= p.table_stride * kBlockTokens && un.z * kBlockTokens < un1.x + kBlockTokens;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -203,163 +321,235 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-
-template <int HG>
-struct Smem {
-  static constexpr int kBoxBytes = HG * kHalves * kBlockTokens * 128;  // one K (or V) box
-  static constexpr int kStageBytes = 2 * kBoxBytes;
+template <int NT>
+struct AttnSmem {
+  static constexpr int kQSlot = 8 * NT * kHeadDim * 2;           // query rows of one unit
+  static constexpr int kPerWarp = kStages * kStageBytes + kQSlot;  // multiple of 1024
+  static constexpr int kOffBars = kWarps * kPerWarp;
+  static constexpr int kBarsPerWarp = kStages + 1;
+  static constexpr int kTotal = kOffBars + kWarps * kBarsPerWarp * 8;
+  static constexpr size_t kDynamic = size_t(kTotal) + 1024;  // + alignment slack
+  static_assert(kPerWarp % 1024 == 0, "per-warp regions must keep 1024-byte alignment");
 };
 
-template <int HG>
-__host__ __device__ constexpr int stages_for() {
-  return HG == 4 ? 3 : (HG == 2 ? 6 : 12);
+// One work unit as a warp sees it (all lanes hold the same values, except `tbl`, `knew`, `vnew`).
+struct Unit {
+  int u;        // unit index, -1 = none (queue exhausted)
+  int b, h, j0, n, split, nsplit, n_ctx;
+  int tbl;      // this lane's block id of the table chunk starting at item `tbase`
+  int tbase;
+  int issued;   // items whose tiles were requested
+  int bf0, bf1, bf2;  // block ids of items 0..2 (from the unit record)
+  int blk_last; // block id of the last item (fused cache write)
+  int last;     // the unit holds the sequence's newest token (fused cache write)
+  uint2 knew;   // this lane's 4 elements of the new K / V row of head h (fused cache write)
+  uint2 vnew;
+};
+
+__device__ __forceinline__ void unit_clear(Unit& x) {
+  x.u = -1;
+  x.b = x.h = x.j0 = x.n = x.split = x.n_ctx = 0;
+  x.nsplit = 1;
+  x.tbl = x.tbase = x.issued = 0;
+  x.bf0 = x.bf1 = x.bf2 = x.blk_last = 0;
+  x.last = 0;
+  x.knew = x.vnew = make_uint2(0u, 0u);
 }
 
-template <int HG>
-__host__ __device__ constexpr size_t attn_smem_bytes() {
-  return size_t(stages_for<HG>()) * Smem<HG>::kStageBytes + 1024 /*align*/ + 1024 /*barriers + combine*/;
-}
-
-template <typename T, int HG, int NT>
-__global__ void __launch_bounds__((HG + 1) * 32, 1)
+template <typename T, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
 decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const AttnParams p) {
-  constexpr int STAGES = stages_for<HG>();
-  constexpr int kBox = Smem<HG>::kBoxBytes;
-  constexpr int kHeadBytes = kHalves * kBlockTokens * 128;  // one head's 16 x 128 tile in a box
-  constexpr int NCONS = HG * 32;
+  using SL = AttnSmem<NT>;
+  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  using Mma = MmaF32<T>;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
-  uint8_t* tiles = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * 2 * kBox);
-  uint64_t* empty = full + STAGES;
-  float* s_mx = reinterpret_cast<float*>(empty + STAGES);  // [64]
-  float* s_inv = s_mx + 64;                                // [64]
-  volatile int* s_flag = reinterpret_cast<volatile int*>(s_inv + 64);  // [0]=last ticket, [1]=abort
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  uint8_t* ring = smem + warp * SL::kPerWarp;
+  T* qslot = reinterpret_cast<T*>(ring + kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL::kOffBars) + warp * SL::kBarsPerWarp;
+  uint64_t* qbar = full + kStages;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], HG);
-    }
-    s_flag[0] = 0;
-    s_flag[1] = 0;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    mbar_init(qbar, 1);
     fence_mbar_init();
+    if (warp == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
   }
-  if (warp == HG && lane == 0) {
-    tma_prefetch_desc(&kmap);
-    tma_prefetch_desc(&vmap);
-  }
-  __syncthreads();
+  __syncwarp();
 
   // Everything below reads data produced by earlier work on the stream.
   pdl_wait_primary();
   pdl_launch_dependents();
 
-  const int num_units = min(max(p.ws.header[0], 0), p.max_units);
+  const int num_units = min(max(p.ws.header[kHdrUnits], 0), p.max_units);
   const int G = p.G;
-  const int NG = p.NG;
-
-  if (warp == HG) {
-    // ------------------------------- producer warp -------------------------------------
-    uint32_t stage = 0, phase = 0;
-    const uint64_t pol = l2_policy_evict_first();
-    bool abort = false;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-      const int4 un = p.ws.units[u];
-      if (!unit_ok(un, u, p)) {
-        if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
-        continue;
-      }
-      const int b = un.x / NG, g = un.x % NG;
-      const int* tb = p.tables + static_cast<int64_t>(b) * p.table_stride;
-      for (int jb = un.y; jb < un.z; jb += 32) {
-        const int cnt = min(32, un.z - jb);
-        const int mine = lane < cnt ? tb[jb + lane] : 0;
-        for (int i = 0; i < cnt; ++i) {
-          const int blk = __shfl_sync(0xffffffffu, mine, i);
-          if (lane == 0) {
-            if (static_cast<unsigned long long>(static_cast<long long>(blk)) >=
-                static_cast<unsigned long long>(p.num_blocks))
-              atomicOr(&g_deverr_attn, AEG_DEVERR_BLOCK_ID_RANGE);  // TMA zero-fills it
-            if (!abort && !mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
-              abort = true;
-              s_flag[1] = 1;
-              atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
-            }
-            if (!abort) {
-              uint8_t* kdst = tiles + stage * 2 * kBox;
-              mbar_arrive_expect_tx(&full[stage], 2 * kBox);
-              tma_load_5d(kdst, &kmap, &full[stage], 0, 0, 0, g * HG, blk, pol);
-              tma_load_5d(kdst + kBox, &vmap, &full[stage], 0, 0, 0, g * HG, blk, pol);
-            }
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-    }
-    // Drain: make sure no bulk copy into this CTA's shared memory is still in flight at exit.
-    if (lane == 0) {
-      for (int s = 0; s < STAGES; ++s) {
-        // The last phase issued on stage s has parity (phase of its last use); waiting on
-        // the empty barrier of each stage means the consumers finished (or gave up).
-        if (!abort && !mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
-          abort = true;
-          atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
-        }
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    }
-    return;
-  }
-
-  // --------------------------------- consumer warps ------------------------------------
-  using Mma = MmaF32<T>;
+  const int Hkv = p.Hkv;
+  const uint64_t pol = l2_policy_evict_first();
   const T* q = static_cast<const T*>(p.q);
   T* out = static_cast<T*>(p.out);
-  const int lr = lane & 7;       // row within an 8x8 matrix
-  const int lm = lane >> 3;      // which of the four matrices this lane addresses
-  const int quad = lane & 3;     // column pair of the accumulator fragment
-  const int grp = lane >> 2;     // row of the accumulator fragment
-  const int cap = p.table_stride * kBlockTokens;
-  const int hgG = HG * G;
+  const int lr = lane & 7;    // row within an 8x8 matrix
+  const int lm = lane >> 3;   // which of the four matrices this lane addresses
+  const int quad = lane & 3;  // column pair of the accumulator fragment
+  const int grp = lane >> 2;  // row of the accumulator fragment
 
-  uint32_t stage = 0, phase = 0;
-  for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-    const int4 un = p.ws.units[u];
-    if (!unit_ok(un, u, p)) continue;
-    const int pair = un.x;
-    const int b = pair / NG, g = pair % NG;
-    const int split = un.w >> 16, nsplit = un.w & 0xffff;
-    const int kvh = g * HG + warp;
-    const int n_ctx = min(max(p.seq_lens[b], 0), cap);
+  bool abort = false;
+  uint32_t g_iss = 0, g_con = 0;  // tiles requested / consumed by this warp
+  uint32_t q_phase = 0;
 
-    // Query fragments (B operand of S^T = K Q^T): Q[head][d] with d contiguous.
+  auto report_timeout = [&]() {
+    abort = true;
+    if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
+  };
+
+  // Unit fetch in three phases so that its latency overlaps the processing of blocks:
+  // A) reserve a unit index, B) load its record, C) unpack it, load the table chunk (and the
+  // new K/V row for the fused write) and start the bulk copy of its query rows.
+  // The first unit of every warp is its global warp index; later ones come from the counter.
+  const int total_warps = static_cast<int>(gridDim.x) * kWarps;
+  bool first_fetch = true;
+  auto phase_a = [&]() -> int {
+    int u = 0;
+    if (first_fetch) {
+      u = static_cast<int>(blockIdx.x) * kWarps + warp;
+      first_fetch = false;
+    } else if (lane == 0) {
+      u = total_warps + atomicAdd(&p.ws.header[kHdrWork], 1);
+    }
+    return u;
+  };
+  auto phase_b = [&](int u_raw, int4& un1) -> int4 {
+    const int u = __shfl_sync(0xffffffffu, u_raw, 0);
+    if (u >= num_units) {
+      un1 = make_int4(0, 0, 0, 0);
+      return make_int4(-1, u, 0, 0);
+    }
+    un1 = p.ws.units[2 * u + 1];
+    return p.ws.units[2 * u];
+  };
+  auto phase_c = [&](int u_raw, const int4& un, const int4& un1, Unit& x) -> bool {  // false: invalid, refetch
+    const int u = __shfl_sync(0xffffffffu, u_raw, 0);
+    unit_clear(x);
+    if (u >= num_units) return true;  // x.u = -1: nothing left
+    if (!unit_ok(un, un1, u, p)) {
+      if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
+      return false;
+    }
+    x.u = u;
+    x.b = un.x / Hkv;
+    x.h = un.x % Hkv;
+    x.j0 = un.y;
+    x.n = un.z - un.y;
+    x.split = un.w >> 16;
+    x.nsplit = un.w & 0xffff;
+    x.n_ctx = un1.x;
+    x.bf0 = un1.y;
+    x.bf1 = un1.z;
+    x.bf2 = un1.w;
+    // table chunk for items 3 .. 34 (items 0..2 come with the record)
+    const int* tb = p.tables + static_cast<int64_t>(x.b) * p.table_stride + x.j0 + 3;
+    x.tbase = 3;
+    x.tbl = lane < min(32, x.n - 3) ? tb[lane] : 0;
+    if (p.fuse_write && x.n > 0 && x.n_ctx > 0 && x.j0 + x.n == (x.n_ctx + kBlockTokens - 1) / kBlockTokens) {
+      // This unit reads the block of position n_ctx - 1: keep the new K/V row of head h to
+      // store it in the cache and patch it into the tile when that block is processed.
+      x.last = 1;
+      const uint32_t* kn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.k_new) +
+                                                             static_cast<int64_t>(x.b) * p.k_new_stride +
+                                                             static_cast<int64_t>(x.h) * kHeadDim) + 2 * lane;
+      const uint32_t* vn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.v_new) +
+                                                             static_cast<int64_t>(x.b) * p.v_new_stride +
+                                                             static_cast<int64_t>(x.h) * kHeadDim) + 2 * lane;
+      x.knew = make_uint2(kn[0], kn[1]);
+      x.vnew = make_uint2(vn[0], vn[1]);
+    }
+    // query rows of this unit into the (now free) query slot
+    const T* qsrc = q + static_cast<int64_t>(x.b) * p.q_stride + static_cast<int64_t>(x.h) * G * kHeadDim;
+    const uint32_t qbytes = G * kHeadDim * 2;
+    fence_proxy_async_smem();
+    if (p.q_bulk) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(qbar, qbytes);
+        bulk_load_1d(qslot, qsrc, qbytes, qbar);
+      }
+    } else {
+      for (int i = lane; i < G * kHeadDim / 2; i += 32)
+        reinterpret_cast<uint32_t*>(qslot)[i] = reinterpret_cast<const uint32_t*>(qsrc)[i];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qbar);
+    }
+    return true;
+  };
+  auto fetch_now = [&](Unit& x) {
+    while (true) {
+      const int ur = phase_a();
+      int4 un1;
+      const int4 un = phase_b(ur, un1);
+      if (phase_c(ur, un, un1, x)) return;
+    }
+  };
+
+  // Requests the next tile of unit x into the ring.
+  auto issue = [&](Unit& x) {
+    const int k = x.issued;
+    int blk;
+    if (k < 3) {
+      blk = k == 0 ? x.bf0 : (k == 1 ? x.bf1 : x.bf2);
+    } else {
+      if (k - x.tbase >= 32) {
+        x.tbase = k;
+        const int* tb = p.tables + static_cast<int64_t>(x.b) * p.table_stride + x.j0 + k;
+        x.tbl = lane < min(32, x.n - k) ? tb[lane] : 0;
+      }
+      blk = __shfl_sync(0xffffffffu, x.tbl, k - x.tbase);
+    }
+    if (k == x.n - 1) x.blk_last = blk;
+    fence_proxy_async_smem();  // the stage being refilled was read through the generic proxy
+    if (lane == 0) {
+      if (static_cast<unsigned long long>(static_cast<long long>(blk)) >= static_cast<unsigned long long>(p.num_blocks))
+        atomicOr(&g_deverr_attn, AEG_DEVERR_BLOCK_ID_RANGE);  // TMA zero-fills it
+      if (!abort) {
+        const uint32_t st = g_iss % kStages;
+        uint8_t* dst = ring + st * kStageBytes;
+        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        tma_load_5d(dst, &kmap, &full[st], 0, 0, 0, x.h, blk, pol);
+        tma_load_5d(dst + kBoxBytes, &vmap, &full[st], 0, 0, 0, x.h, blk, pol);
+      }
+    }
+    ++g_iss;
+    ++x.issued;
+  };
+
+  Unit cur, nxt;
+  unit_clear(nxt);
+  fetch_now(cur);
+  while (cur.u >= 0 && cur.issued < cur.n && g_iss - g_con < kStages) issue(cur);
+
+  while (cur.u >= 0) {
+    // Query fragments (B operand of S^T = K Q^T) from the query slot.
+    if (!abort && !mbar_wait_bounded(qbar, q_phase, kWaitLimitNs)) report_timeout();
+    q_phase ^= 1;
     uint32_t qf[NT][8][2];
-    const T* qb = q + static_cast<int64_t>(b) * p.q_stride + static_cast<int64_t>(kvh) * G * kHeadDim;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int head = nt * 8 + grp;
-      const bool valid = head < G;
+      const bool hv = head < G;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const int d = ks * 16 + 2 * quad;
-        qf[nt][ks][0] = valid ? *reinterpret_cast<const uint32_t*>(qb + head * kHeadDim + d) : 0u;
-        qf[nt][ks][1] = valid ? *reinterpret_cast<const uint32_t*>(qb + head * kHeadDim + d + 8) : 0u;
+        qf[nt][ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qslot + head * kHeadDim + d) : 0u;
+        qf[nt][ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qslot + head * kHeadDim + d + 8) : 0u;
       }
     }
+    __syncwarp();
 
     float o[8][NT][4];
     float m[NT][2], l[NT][2];
@@ -371,19 +561,61 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       for (int mt = 0; mt < 8; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
     }
 
-    for (int j = un.y; j < un.z; ++j) {
-      bool ok = true;
-      if (s_flag[1]) {
-        ok = false;
-      } else if (!mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
-        ok = false;
-        s_flag[1] = 1;
-        if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
+    // Prefetch state of the next unit.
+    int pf = 0, nxt_raw = 0;
+    int4 nxt_un = make_int4(0, 0, 0, 0), nxt_un1 = make_int4(0, 0, 0, 0);
+    bool nxt_ready = false;
+    auto prefetch_step = [&]() {
+      if (pf == 0) {
+        nxt_raw = phase_a();
+      } else if (pf == 1) {
+        nxt_un = phase_b(nxt_raw, nxt_un1);
+      } else if (pf == 2) {
+        if (phase_c(nxt_raw, nxt_un, nxt_un1, nxt)) {
+          nxt_ready = true;
+        } else {
+          pf = -1;  // invalid unit: start over (reported already)
+        }
       }
-      const int nvalid = min(kBlockTokens, n_ctx - j * kBlockTokens);
-      if (ok && nvalid > 0) {
-        const uint32_t kbase = smem_u32(tiles + stage * 2 * kBox) + warp * kHeadBytes;
-        const uint32_t vbase = kbase + kBox;
+      if (pf < 3) ++pf;
+    };
+    auto refill = [&]() {
+      while (g_iss - g_con < kStages) {
+        if (cur.issued < cur.n)
+          issue(cur);
+        else if (nxt_ready && nxt.u >= 0 && nxt.issued < nxt.n)
+          issue(nxt);
+        else
+          break;
+      }
+    };
+
+    for (int k = 0; k < cur.n; ++k) {
+      const uint32_t st = g_con % kStages, ph = (g_con / kStages) & 1;
+      if (!abort && !mbar_wait_bounded(&full[st], ph, kWaitLimitNs)) report_timeout();
+      const int j = cur.j0 + k;
+      const int nvalid = min(kBlockTokens, cur.n_ctx - j * kBlockTokens);
+      if (!abort && nvalid > 0) {
+        const uint32_t kbase = smem_u32(ring + st * kStageBytes);
+        const uint32_t vbase = kbase + kBoxBytes;
+        if (cur.last && k == cur.n - 1) {
+          // Fused cache write: store the newest token's K/V row of head h in the cache (no other
+          // reader of that row in this launch: other warps read other heads' rows) and patch it
+          // into the swizzled tiles, which were fetched before the store.
+          const int t = (cur.n_ctx - 1) % kBlockTokens;
+          if (static_cast<unsigned long long>(static_cast<long long>(cur.blk_last)) <
+              static_cast<unsigned long long>(p.num_blocks)) {
+            const int64_t off = static_cast<int64_t>(cur.blk_last) * p.block_stride +
+                                (static_cast<int64_t>(t) * Hkv + cur.h) * kHeadDim + 4 * lane;
+            *reinterpret_cast<uint2*>(static_cast<T*>(p.k_cache) + off) = cur.knew;
+            *reinterpret_cast<uint2*>(static_cast<T*>(p.v_cache) + off) = cur.vnew;
+          }
+          const int half = lane >> 4, ch = (lane & 15) >> 1;
+          const uint32_t soff = (half * kBlockTokens + t) * 128 + ((ch ^ (t & 7)) << 4) + (lane & 1) * 8;
+          *reinterpret_cast<uint2*>(ring + st * kStageBytes + soff) = cur.knew;
+          *reinterpret_cast<uint2*>(ring + st * kStageBytes + kBoxBytes + soff) = cur.vnew;
+          __syncwarp();
+        }
 
         // S^T[16 tokens][8 heads] per n-tile.
         float s[NT][4];
@@ -402,6 +634,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
         // Online softmax (log2 domain). Column = query head, rows = tokens.
         uint32_t pb[NT][2];
+        uint32_t pl[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const bool v0 = grp < nvalid, v1 = grp + 8 < nvalid;
@@ -430,8 +663,14 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
             o[mt][nt][2] *= a0;
             o[mt][nt][3] *= a1;
           }
-          pb[nt][0] = movmatrix_trans(pack2<T>(p0, p1));
-          pb[nt][1] = movmatrix_trans(pack2<T>(p2, p3));
+          const uint32_t h01 = pack2<T>(p0, p1), h23 = pack2<T>(p2, p3);
+          pb[nt][0] = movmatrix_trans(h01);
+          pb[nt][1] = movmatrix_trans(h23);
+          if constexpr (kSplitP) {
+            const float2 r01 = unpack2<T>(h01), r23 = unpack2<T>(h23);
+            pl[nt][0] = movmatrix_trans(pack2<T>(p0 - r01.x, p1 - r01.y));
+            pl[nt][1] = movmatrix_trans(pack2<T>(p2 - r23.x, p3 - r23.y));
+          }
         }
 
         // O^T[128 dims][8 heads] += V^T P^T.
@@ -443,18 +682,21 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
           uint32_t a[4];
           ldmatrix_x4_trans(a, addr);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Mma::run(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+          for (int nt = 0; nt < NT; ++nt) {
+            Mma::run(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+            if constexpr (kSplitP) Mma::run(o[mt][nt], a, pl[nt][0], pl[nt][1]);
+          }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == STAGES) {
-        stage = 0;
-        phase ^= 1;
-      }
+      ++g_con;
+      prefetch_step();
+      refill();
     }
+    while (pf < 3) prefetch_step();
+    refill();
 
-    // Row sums: each lane holds the sum over its own tokens.
+    // ---- unit result ----
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -462,9 +704,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         l[nt][0] += __shfl_xor_sync(0xffffffffu, l[nt][0], off);
         l[nt][1] += __shfl_xor_sync(0xffffffffu, l[nt][1], off);
       }
-
-    if (nsplit == 1) {
-      T* ob = out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(kvh) * G * kHeadDim;
+    if (cur.nsplit == 1) {
+      T* ob = out + static_cast<int64_t>(cur.b) * p.out_stride + static_cast<int64_t>(cur.h) * G * kHeadDim;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int h0 = nt * 8 + 2 * quad;
@@ -483,12 +724,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
           }
         }
       }
-      continue;
-    }
-
-    // Split unit: write fp32 partials, then take a ticket; the last split merges.
-    {
-      const int64_t base_hl = static_cast<int64_t>(u) * hgG + warp * G;
+    } else {
+      const int64_t base = static_cast<int64_t>(cur.u) * G;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int h0 = nt * 8 + 2 * quad;
@@ -496,64 +733,109 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         for (int mt = 0; mt < 8; ++mt) {
           const int d0 = mt * 16 + grp;
           if (h0 < G) {
-            float* po = p.ws.part_o + (base_hl + h0) * kHeadDim;
+            float* po = p.ws.part_o + (base + h0) * kHeadDim;
             po[d0] = o[mt][nt][0];
             po[d0 + 8] = o[mt][nt][2];
           }
           if (h0 + 1 < G) {
-            float* po = p.ws.part_o + (base_hl + h0 + 1) * kHeadDim;
+            float* po = p.ws.part_o + (base + h0 + 1) * kHeadDim;
             po[d0] = o[mt][nt][1];
             po[d0 + 8] = o[mt][nt][3];
           }
         }
         if (grp == 0) {
-          if (h0 < G) p.ws.part_ml[base_hl + h0] = make_float2(m[nt][0], l[nt][0]);
-          if (h0 + 1 < G) p.ws.part_ml[base_hl + h0 + 1] = make_float2(m[nt][1], l[nt][1]);
+          if (h0 < G) p.ws.part_ml[base + h0] = make_float2(m[nt][0], l[nt][0]);
+          if (h0 + 1 < G) p.ws.part_ml[base + h0 + 1] = make_float2(m[nt][1], l[nt][1]);
         }
       }
     }
+
+    cur = nxt;
+    unit_clear(nxt);
+    refill();
+  }
+
+  // The last warp of the grid to finish resets the work counters for the next launch.
+  if (lane == 0) {
     __threadfence();
-    named_bar(1, NCONS);
-    if (threadIdx.x == 0) {
-      const int old = atomicAdd(&p.ws.counters[pair], 1);
-      s_flag[0] = (old == nsplit - 1) ? 1 : 0;
+    const int done = atomicAdd(&p.ws.header[kHdrExit], 1);
+    if (done == total_warps - 1) {
+      p.ws.header[kHdrWork] = 0;
+      p.ws.header[kHdrExit] = 0;
     }
-    named_bar(1, NCONS);
-    if (s_flag[0]) {
-      __threadfence();
-      const int first = u - split;
-      for (int hl = threadIdx.x; hl < hgG; hl += NCONS) {
-        float mx = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, __ldcg(&p.ws.part_ml[static_cast<int64_t>(first + s) * hgG + hl]).x);
-        float lsum = 0.f;
-        if (mx != -INFINITY)
-          for (int s = 0; s < nsplit; ++s) {
-            const float2 ml = __ldcg(&p.ws.part_ml[static_cast<int64_t>(first + s) * hgG + hl]);
-            lsum += ex2(ml.x - mx) * ml.y;
-          }
-        s_mx[hl] = mx;
-        s_inv[hl] = lsum > 0.f ? 1.f / lsum : 0.f;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Combine kernel: merges the partials of every split (sequence, KV head). Work item =
+// (split pair, query head n of its group), one warp each, no block-level synchronisation:
+// lane c owns float4 column c of the 128-dim row and loads that column of kCombineBatch splits
+// at a time in the same round trip as the splits' (max, sum) pairs; the weights 2^(m_s - M) / L
+// are exchanged by shuffles.
+
+constexpr int kCombineThreads = 128;
+constexpr int kCombineWarps = kCombineThreads / 32;
+constexpr int kCombineBatch = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kCombineThreads)
+decode_combine_kernel(void* out_v, int64_t out_stride, int G, int Hkv, WsPtrs ws) {
+  T* out = static_cast<T*>(out_v);
+  const int lane = threadIdx.x & 31;
+  const int gw = static_cast<int>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
+  const int n_warps = static_cast<int>(gridDim.x) * kCombineWarps;
+  // The split-pair list comes from the plan kernel, which finished before the attention launch
+  // this kernel depends on started; it is read before waiting for the attention results.
+  const int n_items = ws.header[kHdrSplitPairs] * G;
+  int4 sp = gw < n_items ? ws.split_pairs[gw / G] : make_int4(0, 0, 0, 0);
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  const float4* po4 = reinterpret_cast<const float4*>(ws.part_o);
+  for (int item = gw; item < n_items; item += n_warps) {
+    const int n = item % G;
+    const int ns = min(sp.z, kMaxSplits);
+    const int64_t row0 = static_cast<int64_t>(sp.y) * G + n;  // partial row of split 0
+    const float2 a = lane < ns ? __ldcg(&ws.part_ml[row0 + static_cast<int64_t>(lane) * G]) : make_float2(-INFINITY, 0.f);
+    const float2 c = lane + 32 < ns ? __ldcg(&ws.part_ml[row0 + static_cast<int64_t>(lane + 32) * G])
+                                    : make_float2(-INFINITY, 0.f);
+    float4 v[kCombineBatch];
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i)
+      v[i] = i < ns ? __ldcg(po4 + (row0 + static_cast<int64_t>(i) * G) * (kHeadDim / 4) + lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = fmaxf(a.x, c.x);
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w = (M != -INFINITY && a.x != -INFINITY) ? ex2(a.x - M) : 0.f;
+    const float w2 = (M != -INFINITY && c.x != -INFINITY) ? ex2(c.x - M) : 0.f;
+    float L = w * a.y + w2 * c.y;
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < ns; s0 += kCombineBatch) {
+      if (s0 > 0) {
+#pragma unroll
+        for (int i = 0; i < kCombineBatch; ++i)
+          v[i] = s0 + i < ns ? __ldcg(po4 + (row0 + static_cast<int64_t>(s0 + i) * G) * (kHeadDim / 4) + lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      named_bar(1, NCONS);
-      T* ob = out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(g) * hgG * kHeadDim;
-      for (int idx = threadIdx.x; idx < hgG * kHeadDim; idx += NCONS) {
-        const int hl = idx / kHeadDim;
-        const int d = idx - hl * kHeadDim;
-        const float mx = s_mx[hl];
-        float acc = 0.f;
-        if (mx != -INFINITY)
-          for (int s = 0; s < nsplit; ++s) {
-            const int64_t r = static_cast<int64_t>(first + s) * hgG + hl;
-            acc += ex2(__ldcg(&p.ws.part_ml[r]).x - mx) * __ldcg(&p.ws.part_o[r * kHeadDim + d]);
-          }
-        ob[hl * kHeadDim + d] = from_float<T>(acc * s_inv[hl]);
+#pragma unroll
+      for (int i = 0; i < kCombineBatch; ++i) {
+        const float wi = __shfl_sync(0xffffffffu, s0 + i < 32 ? w : w2, (s0 + i) & 31);
+        if (s0 + i < ns) {
+          acc.x += wi * v[i].x;
+          acc.y += wi * v[i].y;
+          acc.z += wi * v[i].z;
+          acc.w += wi * v[i].w;
+        }
       }
-      if (threadIdx.x == 0) {
-        p.ws.counters[pair] = 0;
-        s_flag[0] = 0;
-      }
-      named_bar(1, NCONS);
     }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int b = sp.x / Hkv, h = sp.x % Hkv;
+    T* dst = out + static_cast<int64_t>(b) * out_stride + (static_cast<int64_t>(h) * G + n) * kHeadDim + lane * 4;
+    dst[0] = from_float<T>(acc.x * inv);
+    dst[1] = from_float<T>(acc.y * inv);
+    dst[2] = from_float<T>(acc.z * inv);
+    dst[3] = from_float<T>(acc.w * inv);
+    if (item + n_warps < n_items) sp = ws.split_pairs[(item + n_warps) / G];
   }
 }
 
@@ -576,8 +858,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // 5-D view of one of the K or V caches: (dim-lo 64, token 16, dim-hi D/64, head Hkv, block N).
 // Token comes before dim-hi and head so that the 16 token rows of one (head, dim-half) sit in
 // consecutive 128-byte shared-memory rows, which the 128-byte swizzle spreads over all banks.
-int encode_kv_map(CUtensorMap* map, const void* base, int dtype, int Hkv, int64_t block_stride, int64_t num_blocks,
-                  int hg) {
+int encode_kv_map(CUtensorMap* map, const void* base, int dtype, int Hkv, int64_t block_stride, int64_t num_blocks) {
   auto fn = get_encode_fn();
   if (!fn) return set_error(AEG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const cuuint64_t es = 2;
@@ -585,7 +866,7 @@ int encode_kv_map(CUtensorMap* map, const void* base, int dtype, int Hkv, int64_
                         static_cast<cuuint64_t>(num_blocks)};
   cuuint64_t strides[4] = {static_cast<cuuint64_t>(Hkv) * kHeadDim * es, 64 * es, kHeadDim * es,
                            static_cast<cuuint64_t>(block_stride) * es};
-  cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(kHalves), static_cast<cuuint32_t>(hg), 1};
+  cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(kHalves), 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = fn(map, dtype == AEG_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -594,57 +875,66 @@ int encode_kv_map(CUtensorMap* map, const void* base, int dtype, int Hkv, int64_
   return AEG_OK;
 }
 
-template <typename T, int HG, int NT>
-int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream) {
-  auto kern = decode_attn_kernel<T, HG, NT>;
-  constexpr size_t smem = attn_smem_bytes<HG>();
-  // Per-device one-time set-up (kept out of the launch path so that launches can be captured
-  // into CUDA graphs without further runtime configuration calls).
+// Resident CTAs per SM of the attention kernel (occupancy API, cached per device; the first
+// call on a device also raises the kernel's dynamic shared-memory limit).
+template <typename T, int NT>
+int attn_ctas_per_sm() {
+  auto kern = decode_attn_kernel<T, NT>;
+  constexpr size_t smem = AttnSmem<NT>::kDynamic;
   constexpr int kMaxDevices = 64;
-  static int per_sm_cache[kMaxDevices] = {0};
+  static int cache[kMaxDevices] = {0};
   static std::mutex mu;
   int dev = 0;
-  AEG_CHECK_CUDA(cudaGetDevice(&dev));
-  AEG_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "decode: device ordinal %d out of range", dev);
-  int per_sm = 0;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (per_sm_cache[dev] == 0) {
-      AEG_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      int n = 0;
-      AEG_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (HG + 1) * 32, smem));
-      per_sm_cache[dev] = n > 0 ? n : -1;
-    }
-    per_sm = per_sm_cache[dev];
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) != cudaSuccess || n <= 0)
+      n = -1;
+    cache[dev] = n;
   }
-  if (per_sm < 1) return set_error(AEG_ERR_UNSUPPORTED, "decode attention kernel does not fit on an SM");
+  return cache[dev];
+}
+
+int ctas_per_sm(int dtype, int nt) {
+  if (dtype == AEG_DTYPE_BF16) return nt == 1 ? attn_ctas_per_sm<__nv_bfloat16, 1>() : attn_ctas_per_sm<__nv_bfloat16, 2>();
+  return nt == 1 ? attn_ctas_per_sm<__half, 1>() : attn_ctas_per_sm<__half, 2>();
+}
+
+cudaLaunchAttribute pdl_attr() {
+  cudaLaunchAttribute a{};
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}
+
+template <typename T, int NT>
+int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream) {
+  const int per_sm = attn_ctas_per_sm<T, NT>();
+  if (per_sm < 1) {
+    (void)cudaGetLastError();
+    return set_error(AEG_ERR_CUDA, "decode attention kernel cannot be configured on this device");
+  }
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms() * per_sm));
-  cfg.blockDim = dim3((HG + 1) * 32);
-  cfg.dynamicSmemBytes = smem;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = AttnSmem<NT>::kDynamic;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, km, vm, prm));
+  AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, NT>, km, vm, prm));
+
+  cudaLaunchConfig_t cc{};
+  cc.gridDim = dim3(static_cast<unsigned>(num_sms() * 4));
+  cc.blockDim = dim3(kCombineThreads);
+  cc.dynamicSmemBytes = 0;
+  cc.stream = stream;
+  cc.attrs = attr;
+  cc.numAttrs = 1;
+  AEG_CHECK_CUDA(cudaLaunchKernelEx(&cc, decode_combine_kernel<T>, prm.out, prm.out_stride, prm.G, prm.Hkv, prm.ws));
   return AEG_OK;
-}
-
-template <typename T>
-int launch_attn_dtype(int hg, int nt, const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm,
-                      cudaStream_t s) {
-  if (hg == 4) return nt == 1 ? launch_attn_t<T, 4, 1>(km, vm, prm, s) : launch_attn_t<T, 4, 2>(km, vm, prm, s);
-  if (hg == 2) return nt == 1 ? launch_attn_t<T, 2, 1>(km, vm, prm, s) : launch_attn_t<T, 2, 2>(km, vm, prm, s);
-  return nt == 1 ? launch_attn_t<T, 1, 1>(km, vm, prm, s) : launch_attn_t<T, 1, 2>(km, vm, prm, s);
-}
-
-int ctas_per_sm_for(int hg) {
-  // Resident CTAs per SM of the attention kernel, bounded by its shared memory ring.
-  const size_t smem = hg == 4 ? attn_smem_bytes<4>() : (hg == 2 ? attn_smem_bytes<2>() : attn_smem_bytes<1>());
-  int per = static_cast<int>((228 * 1024) / (smem + 1024));
-  return per < 1 ? 1 : per;
 }
 
 int validate_shape(int B, int Hq, int Hkv, int D, int table_stride) {
@@ -653,8 +943,74 @@ int validate_shape(int B, int Hq, int Hkv, int D, int table_stride) {
   AEG_CHECK_ARG(Hq / Hkv <= 16, "decode: GQA group Hq/Hkv = %d exceeds 16", Hq / Hkv);
   if (D != kHeadDim) return set_error(AEG_ERR_UNSUPPORTED, "decode: head_dim %d not supported (only 128)", D);
   AEG_CHECK_ARG(table_stride > 0, "decode: block-table stride must be positive");
-  AEG_CHECK_ARG(static_cast<int64_t>(B) * (Hkv / pick_hg(Hkv)) < (1 << 30), "decode: batch too large");
+  AEG_CHECK_ARG(static_cast<int64_t>(B) * Hkv < (1 << 30), "decode: batch too large");
   return AEG_OK;
+}
+
+int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_new,
+                  int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
+                  int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
+                  const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream, bool fuse) {
+  int st = validate_shape(B, Hq, Hkv, D, table_stride);
+  if (st != AEG_OK) return st;
+  if (B == 0) return AEG_OK;
+  AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode: dtype %d is not fp16/bf16", dtype);
+  AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode: null pointer");
+  AEG_CHECK_ARG(workspace != nullptr && aligned(workspace, 256), "decode: workspace must be 256-byte aligned");
+  const WsLayout L = ws_layout(B, Hq, Hkv, D);
+  AEG_CHECK_ARG(workspace_bytes >= L.total, "decode: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
+  AEG_CHECK_ARG(num_blocks > 0 && num_blocks <= 0x7fffffffLL, "decode: num_blocks %lld out of range", (long long)num_blocks);
+  AEG_CHECK_ARG(aligned(k_cache, 16) && aligned(v_cache, 16), "decode: K/V cache bases must be 16-byte aligned");
+  AEG_CHECK_ARG(block_stride % 8 == 0 && block_stride >= int64_t(16) * Hkv * D,
+                "decode: block stride %lld must be a multiple of 8 elements and >= 16*Hkv*D", (long long)block_stride);
+  AEG_CHECK_ARG(q_stride >= int64_t(Hq) * D && out_stride >= int64_t(Hq) * D, "decode: q/out token stride < Hq*D");
+  AEG_CHECK_ARG(aligned(q, 4) && q_stride % 2 == 0, "decode: q must be 4-byte aligned with an even token stride");
+  AEG_CHECK_ARG(aligned(out, 2), "decode: out must be 2-byte aligned");
+  AEG_CHECK_ARG(aligned(block_tables, 4) && aligned(seq_lens, 4), "decode: int32 arrays must be aligned");
+  if (fuse) {
+    AEG_CHECK_ARG(k_new && v_new, "decode_layer: null key/value pointer");
+    AEG_CHECK_ARG(k_new_stride >= int64_t(Hkv) * D && v_new_stride >= int64_t(Hkv) * D,
+                  "decode_layer: key/value token stride < Hkv*D");
+    AEG_CHECK_ARG(aligned(k_new, 4) && aligned(v_new, 4) && k_new_stride % 2 == 0 && v_new_stride % 2 == 0,
+                  "decode_layer: key/value must be 4-byte aligned with even token strides");
+  }
+
+  CUtensorMap km, vm;
+  st = encode_kv_map(&km, k_cache, dtype, Hkv, block_stride, num_blocks);
+  if (st != AEG_OK) return st;
+  st = encode_kv_map(&vm, v_cache, dtype, Hkv, block_stride, num_blocks);
+  if (st != AEG_OK) return st;
+
+  AttnParams prm{};
+  prm.out = out;
+  prm.out_stride = out_stride;
+  prm.q = q;
+  prm.q_stride = q_stride;
+  prm.tables = block_tables;
+  prm.table_stride = table_stride;
+  prm.seq_lens = seq_lens;
+  prm.G = Hq / Hkv;
+  prm.Hkv = Hkv;
+  prm.num_pairs = B * Hkv;
+  prm.max_units = L.max_units;
+  prm.num_blocks = num_blocks;
+  prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
+  prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
+  prm.fuse_write = fuse ? 1 : 0;
+  prm.k_new = k_new;
+  prm.v_new = v_new;
+  prm.k_new_stride = k_new_stride;
+  prm.v_new_stride = v_new_stride;
+  prm.k_cache = k_cache;
+  prm.v_cache = v_cache;
+  prm.block_stride = block_stride;
+  prm.ws = ws_ptrs(workspace, L);
+  const int nt = prm.G <= 8 ? 1 : 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == AEG_DTYPE_BF16)
+    return nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(km, vm, prm, s) : launch_attn_t<__nv_bfloat16, 2>(km, vm, prm, s);
+  return nt == 1 ? launch_attn_t<__half, 1>(km, vm, prm, s) : launch_attn_t<__half, 2>(km, vm, prm, s);
 }
 
 }  // namespace
@@ -677,25 +1033,29 @@ size_t aeg_decode_workspace_size(int B, int Hq, int Hkv, int D) {
   return aeg::ws_layout(B, Hq, Hkv, D).total;
 }
 
-int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* seq_lens, int B, int Hq, int Hkv, int D,
-                    int table_stride, void* stream) {
+int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* block_tables, int table_stride,
+                    const int32_t* seq_lens, int B, int Hq, int Hkv, int D, void* stream) {
   int st = aeg::validate_shape(B, Hq, Hkv, D, table_stride);
   if (st != AEG_OK) return st;
   AEG_CHECK_ARG(workspace != nullptr && aeg::aligned(workspace, 256), "decode_plan: workspace must be 256-byte aligned");
   const aeg::WsLayout L = aeg::ws_layout(B, Hq, Hkv, D);
   AEG_CHECK_ARG(workspace_bytes >= L.total, "decode_plan: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
-  AEG_CHECK_ARG(B == 0 || seq_lens != nullptr, "decode_plan: seq_lens is NULL");
-  const int hg = aeg::pick_hg(Hkv);
-  const int ng = Hkv / hg;
-  int target = aeg::num_sms() * aeg::ctas_per_sm_for(hg);
-  if (const char* e = std::getenv("AEG_DECODE_UNITS_PER_CTA")) {
+  AEG_CHECK_ARG(B == 0 || (seq_lens != nullptr && block_tables != nullptr), "decode_plan: seq_lens/block_tables is NULL");
+  AEG_CHECK_ARG(aeg::aligned(seq_lens, 4) && aeg::aligned(block_tables, 4), "decode_plan: int32 arrays must be aligned");
+  // Balanced unit count: a few units per worker warp so that the dynamic scheduler can even
+  // out the tail. AEG_DECODE_UNITS_PER_WARP overrides the factor (tuning experiments).
+  int per_warp = 2;
+  if (const char* e = std::getenv("AEG_DECODE_UNITS_PER_WARP")) {
     const int k = std::atoi(e);
-    if (k > 0) target *= k;
+    if (k > 0) per_warp = k;
   }
+  const int per_sm = aeg::ctas_per_sm(AEG_DTYPE_FP16, (Hq / Hkv) <= 8 ? 1 : 2);
+  long long target = static_cast<long long>(aeg::num_sms()) * (per_sm > 0 ? per_sm : 1) * aeg::kWarps * per_warp;
   if (target > aeg::kMaxTargetUnits) target = aeg::kMaxTargetUnits;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   aeg::WsPtrs w = aeg::ws_ptrs(workspace, L);
-  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, B, ng, table_stride, target, w);
+  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, table_stride,
+                                                          static_cast<int>(target), w);
   AEG_CHECK_LAUNCH("decode_plan");
   return AEG_OK;
 }
@@ -704,49 +1064,19 @@ int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t 
                           const void* v_cache, int64_t block_stride, int64_t num_blocks, const int32_t* block_tables,
                           int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale,
                           int dtype, void* workspace, size_t workspace_bytes, void* stream) {
-  int st = aeg::validate_shape(B, Hq, Hkv, D, table_stride);
-  if (st != AEG_OK) return st;
-  if (B == 0) return AEG_OK;
-  AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode: dtype %d is not fp16/bf16", dtype);
-  AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode: null pointer");
-  AEG_CHECK_ARG(workspace != nullptr && aeg::aligned(workspace, 256), "decode: workspace must be 256-byte aligned");
-  const aeg::WsLayout L = aeg::ws_layout(B, Hq, Hkv, D);
-  AEG_CHECK_ARG(workspace_bytes >= L.total, "decode: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
-  AEG_CHECK_ARG(num_blocks > 0 && num_blocks <= 0x7fffffffLL, "decode: num_blocks %lld out of range", (long long)num_blocks);
-  AEG_CHECK_ARG(aeg::aligned(k_cache, 16) && aeg::aligned(v_cache, 16), "decode: K/V cache bases must be 16-byte aligned");
-  AEG_CHECK_ARG(block_stride % 8 == 0 && block_stride >= int64_t(16) * Hkv * D,
-                "decode: block stride %lld must be a multiple of 8 elements and >= 16*Hkv*D", (long long)block_stride);
-  AEG_CHECK_ARG(q_stride >= int64_t(Hq) * D && out_stride >= int64_t(Hq) * D, "decode: q/out token stride < Hq*D");
-  AEG_CHECK_ARG(aeg::aligned(q, 4) && q_stride % 2 == 0, "decode: q must be 4-byte aligned with an even token stride");
-  AEG_CHECK_ARG(aeg::aligned(out, 2), "decode: out must be 2-byte aligned");
-  AEG_CHECK_ARG(aeg::aligned(block_tables, 4) && aeg::aligned(seq_lens, 4), "decode: int32 arrays must be aligned");
+  return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
+                            const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
+                            Hq, Hkv, D, scale, dtype, workspace, workspace_bytes, stream, false);
+}
 
-  const int hg = aeg::pick_hg(Hkv);
-  CUtensorMap km, vm;
-  st = aeg::encode_kv_map(&km, k_cache, dtype, Hkv, block_stride, num_blocks, hg);
-  if (st != AEG_OK) return st;
-  st = aeg::encode_kv_map(&vm, v_cache, dtype, Hkv, block_stride, num_blocks, hg);
-  if (st != AEG_OK) return st;
-
-  aeg::AttnParams prm{};
-  prm.out = out;
-  prm.out_stride = out_stride;
-  prm.q = q;
-  prm.q_stride = q_stride;
-  prm.tables = block_tables;
-  prm.table_stride = table_stride;
-  prm.seq_lens = seq_lens;
-  prm.G = Hq / Hkv;
-  prm.NG = Hkv / hg;
-  prm.num_pairs = B * prm.NG;
-  prm.max_units = L.max_units;
-  prm.num_blocks = num_blocks;
-  prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
-  prm.ws = aeg::ws_ptrs(workspace, L);
-  const int nt = prm.G <= 8 ? 1 : 2;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == AEG_DTYPE_BF16) return aeg::launch_attn_dtype<__nv_bfloat16>(hg, nt, km, vm, prm, s);
-  return aeg::launch_attn_dtype<__half>(hg, nt, km, vm, prm, s);
+int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* key_new,
+                     int64_t key_stride, const void* value_new, int64_t value_stride, void* k_cache, void* v_cache,
+                     int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
+                     const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  return aeg::decode_common(out, out_stride, q, q_stride, key_new, key_stride, value_new, value_stride, k_cache, v_cache,
+                            block_stride, num_blocks, block_tables, table_stride, seq_lens, B, Hq, Hkv, D, scale, dtype,
+                            workspace, workspace_bytes, stream, true);
 }
 
 }  // extern "C"

@@ -239,21 +239,36 @@ class DecodePlan:
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
         self.table_width: int | None = None
         self.seq_lens: torch.Tensor | None = None
+        self.block_tables: torch.Tensor | None = None
 
-    def plan(self, seq_lens: torch.Tensor, table_width: int) -> "DecodePlan":
-        """Builds the unit list for ``seq_lens`` (int32 CUDA [B]) on the current stream."""
+    def plan(self, seq_lens: torch.Tensor, block_tables: torch.Tensor) -> "DecodePlan":
+        """Builds the unit list for ``seq_lens`` (int32 CUDA [B]) and ``block_tables`` (int32 CUDA
+        [B, W]) on the current stream. Both must stay unchanged while the plan is in use."""
         _require_cuda(seq_lens, "seq_lens")
+        _require_cuda(block_tables, "block_tables")
         if seq_lens.dtype != torch.int32 or seq_lens.dim() != 1 or seq_lens.numel() != self.batch:
             raise ValueError(f"seq_lens must be int32 [{self.batch}]")
+        if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.size(0) != self.batch:
+            raise ValueError(f"block_tables must be int32 [{self.batch}, W]")
+        if block_tables.size(1) == 0:
+            raise ValueError("block_tables has no columns")
         seq_lens = seq_lens.contiguous()
+        if block_tables.stride(1) != 1:
+            block_tables = block_tables.contiguous()
         with torch.cuda.device(self.device):
-            st = lib.aeg_decode_plan(self.workspace.data_ptr(), self.workspace.numel(), seq_lens.data_ptr(),
-                                     self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim, table_width,
-                                     _stream(self.device))
+            st = lib.aeg_decode_plan(self.workspace.data_ptr(), self.workspace.numel(), block_tables.data_ptr(),
+                                     block_tables.stride(0), seq_lens.data_ptr(), self.batch, self.num_q_heads,
+                                     self.num_kv_heads, self.head_dim, _stream(self.device))
         check(st, "decode_plan")
-        self.table_width = table_width
+        self.table_width = block_tables.size(1)
         self.seq_lens = seq_lens
+        self.block_tables = block_tables
         return self
+
+    def matches(self, B: int, Hq: int, Hkv: int, D: int, block_table: torch.Tensor, seq_lens: torch.Tensor) -> bool:
+        return ((self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim) == (B, Hq, Hkv, D)
+                and self.block_tables is not None and self.block_tables.data_ptr() == block_table.data_ptr()
+                and self.seq_lens.data_ptr() == seq_lens.data_ptr() and self.table_width == block_table.size(1))
 
 
 def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
@@ -300,9 +315,9 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
     if W == 0:
         raise ValueError("block_table has no columns")
     if plan is None:
-        plan = DecodePlan(B, Hq, Hkv, D, query.device).plan(cache_seqlens, W)
-    elif (plan.batch, plan.num_q_heads, plan.num_kv_heads, plan.head_dim) != (B, Hq, Hkv, D) or plan.table_width != W:
-        raise ValueError("plan was built for a different batch / head layout / block-table width")
+        plan = DecodePlan(B, Hq, Hkv, D, query.device).plan(cache_seqlens, block_table)
+    elif not plan.matches(B, Hq, Hkv, D, block_table, cache_seqlens):
+        raise ValueError("plan was built for a different batch / head layout / block tables / sequence lengths")
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     dev = query.device
     with torch.cuda.device(dev):
@@ -313,6 +328,73 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
                                        plan.workspace.data_ptr(), plan.workspace.numel(), _stream(dev))
     check(st, "paged_attention_decode")
     return out
+
+
+def decode_layer_flash(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
+                       value_cache: torch.Tensor, block_table: torch.Tensor, cache_seqlens: torch.Tensor,
+                       softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                       plan: DecodePlan | None = None) -> torch.Tensor:
+    """Cache write of each sequence's new token + decode attention, in one launch.
+
+    ``key``/``value`` ``[B, Hkv, D]`` are written at position ``cache_seqlens[b] - 1`` of sequence b
+    (the decode slot the reference builds, ``aegaeon/aegaeon/worker.py:628-633``), then attention runs
+    over ``[0, cache_seqlens[b])``. Same result as ``reshape_and_cache_flash`` with those slots followed
+    by ``flash_attn_decode``.
+    """
+    _require_cuda(query, "query")
+    if query.dim() != 3 or query.stride(2) != 1 or query.stride(1) != query.size(2):
+        raise ValueError("query must be [B, Hq, D] with contiguous heads")
+    _check_paged_view(key_cache, "key_cache")
+    _check_paged_view(value_cache, "value_cache")
+    if key_cache.shape != value_cache.shape or key_cache.stride() != value_cache.stride():
+        raise ValueError("key_cache and value_cache must have the same shape and strides")
+    B, Hq, D = query.shape
+    Hkv = key_cache.size(2)
+    for name, t in (("key", key), ("value", value)):
+        _require_cuda(t, name)
+        if tuple(t.shape) != (B, Hkv, D) or t.stride(2) != 1 or t.stride(1) != D or t.dtype != query.dtype:
+            raise ValueError(f"{name} must be [B, Hkv, D] of the query dtype with contiguous heads")
+    if key_cache.size(3) != D:
+        raise ValueError("head_dim of query and cache differ")
+    if query.dtype not in _DTYPES or key_cache.dtype != query.dtype:
+        raise ValueError("query and caches must share an fp16 or bf16 dtype")
+    _require_cuda(block_table, "block_table")
+    _require_cuda(cache_seqlens, "cache_seqlens")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.size(0) != B:
+        raise ValueError("block_table must be int32 [B, W]")
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    if cache_seqlens.dtype != torch.int32 or cache_seqlens.shape != (B,):
+        raise ValueError("cache_seqlens must be int32 [B]")
+    cache_seqlens = cache_seqlens.contiguous()
+    if out is None:
+        out = torch.empty_like(query, memory_format=torch.contiguous_format)
+    elif out.shape != query.shape or out.dtype != query.dtype or out.stride(2) != 1 or out.stride(1) != D:
+        raise ValueError("out must match query's shape/dtype with contiguous heads")
+    if B == 0:
+        return out
+    if plan is None:
+        plan = DecodePlan(B, Hq, Hkv, D, query.device).plan(cache_seqlens, block_table)
+    elif not plan.matches(B, Hq, Hkv, D, block_table, cache_seqlens):
+        raise ValueError("plan was built for a different batch / head layout / block tables / sequence lengths")
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    dev = query.device
+    with torch.cuda.device(dev):
+        st = lib.aeg_decode_layer(out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0), key.data_ptr(),
+                                  key.stride(0), value.data_ptr(), value.stride(0), key_cache.data_ptr(),
+                                  value_cache.data_ptr(), key_cache.stride(0), key_cache.size(0), block_table.data_ptr(),
+                                  block_table.stride(0), cache_seqlens.data_ptr(), B, Hq, Hkv, D, scale,
+                                  _DTYPES[query.dtype], plan.workspace.data_ptr(), plan.workspace.numel(), _stream(dev))
+    check(st, "decode_layer")
+    return out
+
+
+def decode_layer(out: torch.Tensor, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                 kv_cache: torch.Tensor, layer: int, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                 scale: float, plan: DecodePlan | None = None) -> None:
+    """Fused cache write + decode attention of ``layer`` over Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache."""
+    kc, vc = _layer_views(kv_cache, layer)
+    decode_layer_flash(query, key, value, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan)
 
 
 def paged_attention_decode(out: torch.Tensor, query: torch.Tensor, kv_cache: torch.Tensor, layer: int,

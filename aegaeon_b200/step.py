@@ -27,7 +27,13 @@ class StepShape:
 
 
 class DecodeStep:
-    def __init__(self, kv_cache: torch.Tensor, num_q_heads: int, batch: int, table_width: int, scale: float):
+    """One decode step over an L-layer cache. ``fused=True`` (default) runs each layer as one
+    fused cache-write + attention launch (``ops.decode_layer``, plus its split merge);
+    ``fused=False`` runs the two operators the reference calls per layer (``reshape_and_cache``
+    then ``paged_attention_decode``) with ``slot_mapping`` as given."""
+
+    def __init__(self, kv_cache: torch.Tensor, num_q_heads: int, batch: int, table_width: int, scale: float,
+                 fused: bool = True):
         if kv_cache.dim() != 6:
             raise ValueError("kv_cache must be (N, L, 2, 16, Hkv, D)")
         dev = kv_cache.device
@@ -44,20 +50,26 @@ class DecodeStep:
         self.block_tables = torch.zeros((batch, table_width), dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros((batch,), dtype=torch.int32, device=dev)
         self.plan = ops.DecodePlan(batch, num_q_heads, Hkv, D, dev)
+        self.fused = fused
         self.graph: torch.cuda.CUDAGraph | None = None
 
     @property
     def launches_per_step(self) -> int:
-        """Kernels one step launches: the plan, then a cache write and an attention per layer."""
-        return 1 + 2 * self.shape.num_layers
+        """Kernels one step launches: the plan, then per layer the attention and its split merge
+        (fused) or the cache write, the attention and the merge (unfused)."""
+        return 1 + (2 if self.fused else 3) * self.shape.num_layers
 
     def run_eager(self) -> None:
         """One step on the current stream, op by op."""
-        self.plan.plan(self.seq_lens, self.shape.table_width)
+        self.plan.plan(self.seq_lens, self.block_tables)
         for layer in range(self.shape.num_layers):
-            ops.reshape_and_cache(self.k_new[layer], self.v_new[layer], self.kv_cache, layer, self.slot_mapping)
-            ops.paged_attention_decode(self.out[layer], self.q[layer], self.kv_cache, layer, self.block_tables,
-                                       self.seq_lens, self.scale, plan=self.plan)
+            if self.fused:
+                ops.decode_layer(self.out[layer], self.q[layer], self.k_new[layer], self.v_new[layer], self.kv_cache,
+                                 layer, self.block_tables, self.seq_lens, self.scale, plan=self.plan)
+            else:
+                ops.reshape_and_cache(self.k_new[layer], self.v_new[layer], self.kv_cache, layer, self.slot_mapping)
+                ops.paged_attention_decode(self.out[layer], self.q[layer], self.kv_cache, layer, self.block_tables,
+                                           self.seq_lens, self.scale, plan=self.plan)
 
     def capture(self) -> "DecodeStep":
         """Records one step into a CUDA graph (after one eager warm-up step on a side stream)."""

@@ -118,6 +118,18 @@ def make_layout(cfg: DecodeConfig, rank: int = 0, world: int = 1) -> DecodeLayou
     return DecodeLayout(seq_lens=ctx.astype(np.int32), block_tables=tables, num_blocks=n_pool, seq_ids=ids)
 
 
+def compact_layout(layout: DecodeLayout) -> DecodeLayout:
+    """The same sequences over a pool that holds only their blocks (ids 0..total-1, in table order)."""
+    nb = (layout.seq_lens.astype(np.int64) + BLOCK_SIZE - 1) // BLOCK_SIZE
+    tables = np.zeros_like(layout.block_tables)
+    off = 0
+    for i, n in enumerate(nb):
+        tables[i, :n] = np.arange(off, off + n)
+        off += n
+    return DecodeLayout(seq_lens=layout.seq_lens.copy(), block_tables=tables, num_blocks=max(int(off), 1),
+                        seq_ids=layout.seq_ids.copy())
+
+
 def new_token_slots(layout: DecodeLayout) -> np.ndarray:
     """Slot of each sequence's newest position ``ctx - 1`` (written before the layer's attention)."""
     pos = layout.seq_lens.astype(np.int64) - 1

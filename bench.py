@@ -3,8 +3,9 @@
 
 Default workload (``--config cfg2``): one Qwen2.5-7B decode step = 28 layers x (reshape_and_cache
 of one new token per sequence + paged decode attention), batch 64, lognormal contexts, a pool of
-16384 blocks (15 GB fp16). A step is captured once as a CUDA graph (plan + 56 kernels) and
-replayed; the KV read per step (1.6 GB) is far larger than the 126 MB L2, so no flush is needed.
+16384 blocks (15 GB fp16). A step is captured once as a CUDA graph (the plan, then per layer the
+fused cache-write/attention launch and its split merge) and replayed; the KV read per step
+(1.6 GB) is far larger than the 126 MB L2, so no flush is needed.
 
 One JSON line on rank 0 (see the keys below). ``--impl reference`` times the CPU restatement of
 the reference's path (the oracle, all host threads) on the same workload.
@@ -44,6 +45,12 @@ def _args():
     p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    p.add_argument("--unfused", action="store_true",
+                   help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
+    p.add_argument("--compact-pool", action="store_true",
+                   help="size the block pool to the blocks the batch uses (same kernels; small-case profiling)")
+    p.add_argument("--profile-run", action="store_true",
+                   help="timed graph replays only: no clock pre-roll, per-launch timing, end-to-end or CPU leg")
     return p.parse_args()
 
 
@@ -259,13 +266,15 @@ def run_decode(args, world, rank, local):
     else:
         lay = synth.make_layout(cfg)
         scaling = "weak"
+    if args.compact_pool:
+        lay = synth.compact_layout(lay)
     B = len(lay.seq_lens)
     L, Hq, Hkv, D = cfg.num_layers, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
     scale = synth.default_scale(cfg)
 
     kv = torch.empty((lay.num_blocks, L, 2, 16, Hkv, D), dtype=cfg.dtype, device=device)
     synth.fill_normal_(kv, cfg.value_std, cfg.seed + 1000 * rank)
-    step = DecodeStep(kv, Hq, B, lay.width, scale)
+    step = DecodeStep(kv, Hq, B, lay.width, scale, fused=not args.unfused)
     g = torch.Generator(device=device).manual_seed(cfg.seed + 17 + rank)
     dev_inputs = dict(
         q=(torch.randn(step.q.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
@@ -285,6 +294,14 @@ def run_decode(args, world, rank, local):
         step.replay()
     torch.cuda.synchronize(device)
 
+    if args.profile_run:
+        for _ in range(args.steps):
+            step.replay()
+        torch.cuda.synchronize(device)
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "config": cfg.name, "steps": args.steps,
+                              "pool_blocks": lay.num_blocks}), flush=True)
+        return
     clocks = ClockSampler(device)
     # Untimed pre-roll of ~1 s so that the clock samples cover the GPU under this load.
     t_pre = time.perf_counter()
@@ -306,20 +323,27 @@ def run_decode(args, world, rank, local):
     ms = _max_over_ranks(e0.elapsed_time(e1), world, device)
     clock_info = clocks.stop()
 
-    # Per-launch durations of the dominant kernel (attention) and of the cache write.
+    # Per-launch durations of the dominant kernel (the layer's attention launch with its split
+    # merge; fused with the cache write unless --unfused) and of the separate cache write.
     n_prof = max(1, min(args.steps, 8))
     attn_fns, write_fns = [], []
     for _ in range(n_prof):
         for layer in range(L):
-            attn_fns.append(lambda l=layer: ops.paged_attention_decode(step.out[l], step.q[l], kv, l, step.block_tables,
-                                                                       step.seq_lens, scale, plan=step.plan))
+            if step.fused:
+                attn_fns.append(lambda l=layer: ops.decode_layer(step.out[l], step.q[l], step.k_new[l], step.v_new[l],
+                                                                 kv, l, step.block_tables, step.seq_lens, scale,
+                                                                 plan=step.plan))
+            else:
+                attn_fns.append(lambda l=layer: ops.paged_attention_decode(step.out[l], step.q[l], kv, l,
+                                                                           step.block_tables, step.seq_lens, scale,
+                                                                           plan=step.plan))
             write_fns.append(lambda l=layer: ops.reshape_and_cache(step.k_new[l], step.v_new[l], kv, l,
                                                                    step.slot_mapping))
     attn_ms = []
     for s in range(n_prof):
         attn_ms += _per_launch_ms(attn_fns[s * L:(s + 1) * L], device)
     write_ms = _per_launch_ms(write_fns[:L], device)
-    plan_ms = _per_launch_ms([lambda: step.plan.plan(step.seq_lens, lay.width)] * 4, device)
+    plan_ms = _per_launch_ms([lambda: step.plan.plan(step.seq_lens, step.block_tables)] * 4, device)
 
     # End to end through the public step API with host buffers.
     for _ in range(2):
@@ -344,7 +368,8 @@ def run_decode(args, world, rank, local):
     value = tokens_total / (ms_step / 1e3)
     kv_step = algo["kv_read"] * L
     attn_avg_ms = statistics.mean(attn_ms)
-    achieved = algo["attention"] / (attn_avg_ms / 1e3) / 1e9
+    launch_bytes = algo["attention"] + (algo["reshape_and_cache"] if step.fused else 0)
+    achieved = launch_bytes / (attn_avg_ms / 1e3) / 1e9
     peak, peak_src = _peaks()
     traffic = _ncu_traffic(f"decode_attn_{cfg.name}")
 
@@ -369,7 +394,9 @@ def run_decode(args, world, rank, local):
             "kv_bytes_per_step": kv_step, "accumulate": "fp32",
             "l2": f"inputs larger than L2: {kv_step / 1e9:.2f} GB of K/V read per step vs 126 MB L2 (no flush)",
             "parallelism": f"{world} GPU(s), one process each, own pool and batch, no collective",
-            "launch": "one CUDA graph per step (plan + per-layer cache write + attention, PDL)",
+            "launch": ("one CUDA graph per step: plan + per layer one fused cache-write/attention launch and its "
+                       "split merge (PDL)" if step.fused else
+                       "one CUDA graph per step: plan + per layer reshape_and_cache, attention, split merge (PDL)"),
         },
         "kv_read_gbs": kv_step * world / (ms_step / 1e3) / 1e9,
         "hbm_frac_step": (algo["attention"] + algo["reshape_and_cache"]) * L / (ms_step / 1e3) / 1e9 / peak,
@@ -384,18 +411,18 @@ def run_decode(args, world, rank, local):
         "gpu_launches": args.steps * step.launches_per_step,
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_attn_kernel",
+            "kernel": "decode_attn_kernel (+ decode_combine_kernel, timed together per layer call)",
             "achieved": achieved,
             "peak": peak,
             "unit": "GB/s",
             "frac": achieved / peak,
             "peak_source": peak_src,
             "traffic": traffic,
-            "algorithmic_bytes_per_launch": algo["attention"],
+            "algorithmic_bytes_per_launch": launch_bytes,
             "avg_launch_us": attn_avg_ms * 1e3,
             "launches_timed": len(attn_ms),
-            "reshape_and_cache_avg_us": statistics.mean(write_ms) * 1e3,
-            "plan_avg_us": statistics.mean(plan_ms) * 1e3,
+            "reshape_and_cache_median_us": statistics.median(write_ms) * 1e3,
+            "plan_median_us": statistics.median(plan_ms) * 1e3,
         },
         "clocks": clock_info,
     }

@@ -138,27 +138,46 @@ AEG_API int aeg_reshape_and_cache(const void* key, const void* value, int64_t ke
  *   blk(b, j) = block_tables[b * table_stride + j / 16]
  * computed in fp32 and rounded to the storage dtype. seq_len 0 gives a zero row.
  *
- * A decode step runs aeg_decode_plan once (it depends only on seq_lens, like the per-step
- * attention metadata at worker.py:694-711) and then aeg_paged_attn_decode once per layer
- * with the same workspace. The workspace is caller-owned device memory of at least
- * aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by one stream at
- * a time. The plan splits every (sequence, kv-head group) into block ranges of balanced size
- * so that all SMs stream the same number of KV bytes; split results are merged inside the
- * attention launch by the last CTA to finish each sequence.
+ * A decode step runs aeg_decode_plan once (it depends only on seq_lens and block_tables, like
+ * the per-step attention metadata at worker.py:694-711) and then aeg_paged_attn_decode (or
+ * aeg_decode_layer) once per layer with the same workspace. The workspace is caller-owned device
+ * memory of at least aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by
+ * one stream at a time. The plan cuts every (sequence, KV head) into block ranges of near-equal
+ * length (longest first), which the warps of a persistent kernel take from an atomic counter;
+ * ranges of a split (sequence, head) are merged by a second kernel that the attention call
+ * enqueues right after itself.
  *
  * Supported: D = 128; Hq % Hkv == 0; Hq / Hkv <= 16; fp16 or bf16; 16-byte aligned K/V
- * bases and block stride; q/out token strides that are multiples of 8 elements.
+ * bases; a block stride that is a multiple of 8 elements; q/out with even token strides.
  */
 AEG_API size_t aeg_decode_workspace_size(int B, int Hq, int Hkv, int D);
 
-AEG_API int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* seq_lens, int B,
-                    int Hq, int Hkv, int D, int table_stride, void* stream);
+AEG_API int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* block_tables,
+                            int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv, int D,
+                            void* stream);
 
 AEG_API int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                           const void* k_cache, const void* v_cache, int64_t block_stride,
                           int64_t num_blocks, const int32_t* block_tables, int table_stride,
                           const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale,
                           int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* a6 + a7 fused. One decode layer as the reference runs it per layer (cache write of the new
+ * token, then decode attention; aegaeon/aegaeon/worker.py:517-523): for every sequence b with
+ * n = seq_lens[b] > 0, the new token's key/value rows (key_new[b], value_new[b], [Hkv, D] each,
+ * token strides key_stride/value_stride) are written into position n - 1 of the sequence, i.e.
+ * slot block_tables[b][(n-1)/16] * 16 + (n-1) % 16 -- the slot the reference builds for a decode
+ * request (worker.py:628-633 with context_len = seq_len - 1) -- and attention then runs over
+ * positions [0, n) exactly as aeg_paged_attn_decode, in the same launch. The result equals
+ * aeg_reshape_and_cache with those slots followed by aeg_paged_attn_decode.
+ * key_new/value_new must be 4-byte aligned with even token strides. */
+AEG_API int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                             const void* key_new, int64_t key_stride, const void* value_new,
+                             int64_t value_stride, void* k_cache, void* v_cache,
+                             int64_t block_stride, int64_t num_blocks, const int32_t* block_tables,
+                             int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv,
+                             int D, float scale, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

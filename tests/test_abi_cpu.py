@@ -21,7 +21,7 @@ def _declared_symbols():
 def test_header_declares_the_path():
     syms = _declared_symbols()
     for name in ("aeg_swap", "aeg_swap_sm", "aeg_copy_blocks", "aeg_reshape_and_cache", "aeg_decode_plan",
-                 "aeg_paged_attn_decode", "aeg_decode_workspace_size", "aeg_last_error", "aeg_read_device_errors"):
+                 "aeg_paged_attn_decode", "aeg_decode_layer", "aeg_decode_workspace_size", "aeg_last_error", "aeg_read_device_errors"):
         assert name in syms
 
 
@@ -73,18 +73,18 @@ def test_decode_validation_on_host():
     lib = _native.lib
     p, _k = _fake()
     # unsupported head dim
-    st = lib.aeg_decode_plan(p, 1 << 30, p, 4, 28, 4, 64, 16, None)
+    st = lib.aeg_decode_plan(p, 1 << 30, p, 16, p, 4, 28, 4, 64, None)
     assert st == _native.AEG_ERR_UNSUPPORTED and "head_dim" in _native.last_error()
     # GQA group too large
-    st = lib.aeg_decode_plan(p, 1 << 30, p, 4, 68, 4, 128, 16, None)
+    st = lib.aeg_decode_plan(p, 1 << 30, p, 16, p, 4, 68, 4, 128, None)
     assert st == _native.AEG_ERR_INVALID_ARGUMENT
     # misaligned workspace
-    st = lib.aeg_decode_plan(p + 1, 1 << 30, p, 4, 28, 4, 128, 16, None)
+    st = lib.aeg_decode_plan(p + 1, 1 << 30, p, 16, p, 4, 28, 4, 128, None)
     assert st == _native.AEG_ERR_INVALID_ARGUMENT and "aligned" in _native.last_error()
     # workspace too small
     need = lib.aeg_decode_workspace_size(4, 28, 4, 128)
     aligned = (p + 255) // 256 * 256
-    st = lib.aeg_decode_plan(aligned, need - 1, p, 4, 28, 4, 128, 16, None)
+    st = lib.aeg_decode_plan(aligned, need - 1, p, 16, p, 4, 28, 4, 128, None)
     assert st == _native.AEG_ERR_INVALID_ARGUMENT and "need" in _native.last_error()
     # attention: bad dtype, misaligned cache base
     args = dict(out=p, q=p, k=p, v=p)

@@ -1,0 +1,63 @@
+"""Pins the CPU oracle to golden vectors produced by vLLM's own kernels (no GPU needed).
+
+The reference runs decode attention and the cache write through vLLM 0.5.1's FlashAttention
+backend (un-vendored). ``tests/golden/make_golden.py`` ran the same kernel family from the
+installed vLLM (``reshape_and_cache_flash`` + ``vllm_flash_attn.flash_attn_varlen_func`` with a
+block table, FA2) on per-layer views of Aegaeon's interleaved cache and saved inputs/outputs.
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+CASES = ["vllm_cfg1_fp16.npz", "vllm_gqa8_bf16.npz"]
+
+
+def _load(name):
+    path = os.path.join(HERE, name)
+    if not os.path.exists(path):
+        pytest.fail(f"golden fixture {name} missing (generate with tests/golden/make_golden.py)")
+    return dict(np.load(path))
+
+
+def _write_new_tokens(g):
+    cache = g["cache_before"].copy()
+    N, L, _, _, Hkv, D = cache.shape
+    layer = int(g["layer"])
+    flat = cache.reshape(-1)
+    rc = orc.c_reshape_and_cache(g["k_new"], g["v_new"], flat[(layer * 2) * 16 * Hkv * D:],
+                                 flat[(layer * 2 + 1) * 16 * Hkv * D:], L * 2 * 16 * Hkv * D, N, g["slot_mapping"])
+    assert rc == 0
+    return cache
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_cache_write_matches_vllm(name):
+    g = _load(name)
+    cache = _write_new_tokens(g)
+    # bit-exact against vLLM's cache after its write (padding slot -1 skipped)
+    assert hashlib.sha256(cache.tobytes()).hexdigest() == str(g["cache_after_sha256"])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_attention_matches_vllm(name):
+    g = _load(name)
+    cache = _write_new_tokens(g)
+    N, L, _, _, Hkv, D = cache.shape
+    layer = int(g["layer"])
+    dt = orc.BF16 if str(g["dtype"]) == "bf16" else orc.FP16
+    flat = cache.reshape(-1)
+    bs = L * 2 * 16 * Hkv * D
+    got = orc.c_paged_attention(g["q"], flat[(layer * 2) * 16 * Hkv * D:], flat[(layer * 2 + 1) * 16 * Hkv * D:], bs,
+                                g["tables"], g["seq_lens"], Hkv, float(g["scale"]), dt)
+    ok, err, excess = orc.compare_attention(g["out_vllm"], got, dt)  # vLLM vs oracle, atol 2e-3 / rtol 1e-2
+    assert ok, (err, excess)
+    # the numpy restatement agrees as well
+    npo = orc.np_paged_attention(g["q"], cache[:, layer, 0], cache[:, layer, 1], g["tables"], g["seq_lens"],
+                                 float(g["scale"]), dt)
+    ok2, err2, _ = orc.compare_attention(g["out_vllm"], npo, dt)
+    assert ok2, err2
