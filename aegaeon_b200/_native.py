@@ -48,6 +48,9 @@ SIGNATURES = {
     "aeg_decode_layer": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p,
                                 _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,
                                 ctypes.c_float, _i32, _c_void_p, _sz, _c_void_p]),
+    "aeg_paged_attn_decode_noalloc": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64,
+                                             _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, ctypes.c_float,
+                                             _i32, _c_void_p]),
 }
 
 

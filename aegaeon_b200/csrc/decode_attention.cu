@@ -951,14 +951,14 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
                   int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
                   int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
                   const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
-                  size_t workspace_bytes, void* stream, bool fuse) {
+                  size_t workspace_bytes, void* stream, bool fuse, const WsLayout* layout = nullptr) {
   int st = validate_shape(B, Hq, Hkv, D, table_stride);
   if (st != AEG_OK) return st;
   if (B == 0) return AEG_OK;
   AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode: dtype %d is not fp16/bf16", dtype);
   AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode: null pointer");
   AEG_CHECK_ARG(workspace != nullptr && aligned(workspace, 256), "decode: workspace must be 256-byte aligned");
-  const WsLayout L = ws_layout(B, Hq, Hkv, D);
+  const WsLayout L = layout ? *layout : ws_layout(B, Hq, Hkv, D);
   AEG_CHECK_ARG(workspace_bytes >= L.total, "decode: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
   AEG_CHECK_ARG(num_blocks > 0 && num_blocks <= 0x7fffffffLL, "decode: num_blocks %lld out of range", (long long)num_blocks);
   AEG_CHECK_ARG(aligned(k_cache, 16) && aligned(v_cache, 16), "decode: K/V cache bases must be 16-byte aligned");
@@ -1011,6 +1011,84 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   if (dtype == AEG_DTYPE_BF16)
     return nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(km, vm, prm, s) : launch_attn_t<__nv_bfloat16, 2>(km, vm, prm, s);
   return nt == 1 ? launch_attn_t<__half, 1>(km, vm, prm, s) : launch_attn_t<__half, 2>(km, vm, prm, s);
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free decode attention (aeg_paged_attn_decode_noalloc).
+//
+// Some callers cannot hand this library a workspace and must not make it allocate one: a host
+// that binds only the C ABI and owns no device allocator, code that runs inside an allocator
+// or memory-pool callback (where allocating again would recurse into the allocator), and
+// serving loops whose device memory has all been handed to the KV-block pool up front, so a
+// cudaMalloc there would fail or evict cache blocks. For them this entry plans and runs the
+// attention in a fixed scratch area held in this module's own static device memory. The
+// driver reserves it, once per device, when it loads the module; the call itself allocates
+// nothing.
+//
+// Limits and rules of use:
+//   * The scratch holds kNoAllocScratchBytes (32 MiB) per device. Its layout is the workspace
+//     layout with room for the units the plan actually makes (target + B*Hkv, where the target
+//     is the one aeg_decode_plan uses by default), so the need grows with B*Hkv and the GQA
+//     group: about 9.6 MB for 64 sequences x 4 KV heads x 7 query heads each. A call that
+//     would need more is rejected with AEG_ERR_INVALID_ARGUMENT before anything is enqueued.
+//   * Nothing in the scratch has to start at zero for the first call: the plan kernel that
+//     every call enqueues writes the whole header, including the work and exit counters that
+//     the attention kernel needs at zero, and the last warp of the attention kernel sets them
+//     back to zero. (Static device memory also starts zeroed when the module is loaded.)
+//   * One scratch per device means calls on one device must not overlap: two calls in flight
+//     at once on different streams race on the plan, the counters and the partials. Issue
+//     them on one stream, or order the streams.
+//   * The first call on a device does one-time set-up with that device current: it looks up
+//     the scratch address (cudaGetSymbolAddress, which may load the module) and configures
+//     the attention kernel's shared-memory limit. Make that first call before any stream
+//     capture begins.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices];
+
+// Device address of the current device's scratch, looked up once per device.
+int noalloc_scratch(void** ptr) {
+  int dev = 0;
+  AEG_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(AEG_ERR_UNSUPPORTED, "decode_noalloc: device ordinal %d >= %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      return set_error(AEG_ERR_CUDA, "decode_noalloc: cudaGetSymbolAddress of the scratch failed on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return AEG_OK;
+}
+
+// The workspace layout with room for max_units units (the regular layout reserves
+// kMaxTargetUnits + B*Hkv, far more than the default plan makes).
+WsLayout noalloc_layout(int B, int Hq, int Hkv, int D, int max_units) {
+  WsLayout w{};
+  const int G = Hq / Hkv;
+  const int64_t P = int64_t(B) * Hkv;
+  w.max_units = max_units;
+  size_t off = 256;
+  w.split_pairs = off;
+  off = align256(off + sizeof(int4) * P);
+  w.units = off;
+  off = align256(off + 2 * sizeof(int4) * size_t(max_units));
+  w.part_ml = off;
+  off = align256(off + sizeof(float2) * size_t(max_units) * G);
+  w.part_o = off;
+  off = align256(off + sizeof(float) * size_t(max_units) * G * D);
+  w.total = off;
+  return w;
 }
 
 }  // namespace
@@ -1077,6 +1155,39 @@ int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64_t q_str
   return aeg::decode_common(out, out_stride, q, q_stride, key_new, key_stride, value_new, value_stride, k_cache, v_cache,
                             block_stride, num_blocks, block_tables, table_stride, seq_lens, B, Hq, Hkv, D, scale, dtype,
                             workspace, workspace_bytes, stream, true);
+}
+
+// Plan + attention + split merge in the static per-device scratch (no counterpart in the
+// reference; see the allocation-free section above for limits and rules of use).
+int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_cache,
+                                  const void* v_cache, int64_t block_stride, int64_t num_blocks,
+                                  const int32_t* block_tables, int table_stride, const int32_t* seq_lens, int B, int Hq,
+                                  int Hkv, int D, float scale, int dtype, void* stream) {
+  int st = aeg::validate_shape(B, Hq, Hkv, D, table_stride);
+  if (st != AEG_OK) return st;
+  if (B == 0) return AEG_OK;
+  AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode_noalloc: dtype %d is not fp16/bf16", dtype);
+  AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode_noalloc: null pointer");
+  AEG_CHECK_ARG(aeg::aligned(seq_lens, 4) && aeg::aligned(block_tables, 4), "decode_noalloc: int32 arrays must be aligned");
+  const int per_sm = aeg::ctas_per_sm(AEG_DTYPE_FP16, (Hq / Hkv) <= 8 ? 1 : 2);
+  long long target = static_cast<long long>(aeg::num_sms()) * (per_sm > 0 ? per_sm : 1) * aeg::kWarps * 2;
+  if (target > aeg::kMaxTargetUnits) target = aeg::kMaxTargetUnits;
+  const aeg::WsLayout L =
+      aeg::noalloc_layout(B, Hq, Hkv, D, static_cast<int>(target + static_cast<long long>(B) * Hkv));
+  AEG_CHECK_ARG(L.total <= aeg::kNoAllocScratchBytes,
+                "decode_noalloc: B=%d, Hq=%d, Hkv=%d needs %zu bytes of scratch, more than the %zu bytes of the "
+                "static scratch; use aeg_paged_attn_decode with a caller-owned workspace",
+                B, Hq, Hkv, L.total, aeg::kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  st = aeg::noalloc_scratch(&scratch);
+  if (st != AEG_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, table_stride,
+                                                          static_cast<int>(target), aeg::ws_ptrs(scratch, L));
+  AEG_CHECK_LAUNCH("decode_plan (noalloc)");
+  return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
+                            const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
+                            Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, stream, false, &L);
 }
 
 }  // extern "C"

@@ -179,6 +179,27 @@ AEG_API int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64
                              int D, float scale, int dtype, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Allocation-free decode attention. No counterpart in the reference: Aegaeon always has torch's
+ * allocator at hand. This entry serves callers that cannot pass a workspace and must not have the
+ * library allocate one -- hosts binding only this C ABI with no device allocator of their own,
+ * code running inside an allocator or memory-pool callback, serving loops whose device memory is
+ * all given to the KV-block pool. It computes what aeg_decode_plan + aeg_paged_attn_decode compute
+ * (same arguments minus the workspace) in a fixed 32 MiB scratch area per device that lives in the
+ * library's static device memory; nothing is allocated by the call.
+ *   - Limit: the scratch need grows with B*Hkv and Hq/Hkv (about 9.6 MB for B=64, Hkv=4, Hq=28);
+ *     a call needing more than 32 MiB fails with AEG_ERR_INVALID_ARGUMENT, nothing enqueued.
+ *   - Nothing has to be zeroed by the caller: every call re-plans and resets the counters it uses.
+ *   - The scratch is shared by all calls on a device: calls that overlap in time (e.g. on two
+ *     unordered streams) race. Keep them on one stream or order them.
+ *   - The first call on a device looks up the scratch address and configures the kernel with that
+ *     device current; make it before any stream capture begins. */
+AEG_API int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q,
+                                          int64_t q_stride, const void* k_cache, const void* v_cache,
+                                          int64_t block_stride, int64_t num_blocks,
+                                          const int32_t* block_tables, int table_stride,
+                                          const int32_t* seq_lens, int B, int Hq, int Hkv, int D,
+                                          float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
