@@ -42,7 +42,7 @@ int set_error(int code, const char* fmt, ...);
       return ::aeg::set_error(AEG_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(_e)); \
   } while (0)
 
-inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+__host__ __device__ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // Number of SMs of the current device (cached per device).
 int num_sms();

@@ -7,31 +7,38 @@
 // KV head h / (Hq / Hkv).
 //
 // Design (memory-bound: every K/V byte is read exactly once per layer call):
-//   * Work unit = (sequence b, KV head h, range of 16-token blocks). A plan kernel, run once
-//     per decode step, cuts every (b, h) into ranges of near-equal length (at most kMaxSplits)
-//     and orders the units longest first. A unit record also carries the sequence length and
-//     the unit's first three block ids.
-//   * Every warp is an independent worker (kWarps per CTA, one CTA per SM). Its first unit is
-//     its warp index, later ones come from an atomic work counter (dynamic load balance; the
-//     last warp to exit resets it for the next launch). It streams each (block, head) K and V
-//     tile (16 tokens x 128 dims, 4 KiB each) into its own kStages-deep shared-memory ring with
-//     5-D bulk-tensor TMA loads (128-byte swizzle, evict-first L2 policy) completing on
-//     mbarriers. The next unit's record, block-table chunk and query rows (1-D bulk copy) are
-//     prefetched one phase per processed block, and the ring keeps streaming across unit
-//     boundaries. No CTA-wide barrier is taken after set-up.
+//   * Work item = one 16-token block of one (sequence b, KV head h) pair. A plan kernel, run
+//     once per decode step, cuts the batch's items (in pair order) into W contiguous ranges of
+//     equal size, one per worker warp of the attention grid (W = 8 warps x one CTA per SM).
+//     A worker's range is a list of units (pieces of pairs); a pair cut by a worker start is
+//     "split", and its units write partials. A unit record carries the pair, its block range,
+//     its partial slot, the sequence length and its first three block ids.
+//   * Every warp works through its own range with no scheduling traffic: its unit records sit
+//     in its lanes (one load for the first, one coalesced load for the next 31), so moving on
+//     to the next unit needs no global round trip. It streams each (block, head) K and V tile
+//     (16 tokens x 128 dims, 4 KiB each) into its own kStages-deep shared-memory ring with 5-D
+//     bulk-tensor TMA loads (128-byte swizzle, evict-first L2 policy) completing on
+//     mbarriers, kStages tiles ahead of the compute, across unit boundaries. The next unit's
+//     query rows are bulk-copied while the current unit is computed.
 //   * Per block the warp computes S^T = K Q^T with mma.sync m16n8k16 (16 tokens x 8 query
 //     heads of the GQA group; K fragments by ldmatrix from the swizzled tile), an fp32 online
 //     softmax in the exp2 domain with quad shuffles, transposes P in registers with movmatrix
 //     and accumulates O^T += V^T P^T (V fragments by ldmatrix.trans). For bf16, P enters as a
 //     bf16 value plus its bf16 rounding residue (two MMAs) so that P V keeps ~16 mantissa bits.
-//   * A unit covering a whole (b, h) writes the output rows; a split unit writes an fp32
-//     partial (O scaled by 2^-max, max, sum). A combine kernel, launched right after with
-//     programmatic dependent launch, merges the partials of every split (b, h): one warp per
-//     (b, h, query head), all of its loads in one or two round trips.
+//   * A whole pair's unit writes the output rows; a split unit writes an fp32 partial (O scaled
+//     by 2^-max, max, sum). When its range is done every thread publishes its partials (one
+//     fence), the CTA's warps meet, and one thread per CTA arrives at a grid-wide barrier (the
+//     grid is launched cooperatively). Then all warps merge the split pairs: a merge item is
+//     (pair, query head, dimension chunk), sized so that every lane loads at most 16 pieces in
+//     one round trip, and the plan spreads the items evenly over the warps. Measured and
+//     rejected: signalling every split (fence + counter per split, the last one merges) cost
+//     ~2.5 us per split under full HBM load; merging each pair in the CTA that computed its
+//     last piece (per-CTA flags, no grid barrier) piled the long and the short-sequence pairs
+//     onto a few CTAs; a dynamic unit queue left ~2 us gaps at every unit change.
 //   * Fused form (aeg_decode_layer): the warp that reads a sequence's newest block writes the
 //     new token's K/V row of its head into the cache and patches it into the tile.
-//   * Every mbarrier wait is bounded (2 s); a timeout raises AEG_DEVERR_WAIT_TIMEOUT and the
-//     warp drains instead of hanging.
+//   * Every wait is bounded (2 s); a timeout raises AEG_DEVERR_WAIT_TIMEOUT and the warp
+//     drains instead of hanging.
 #include "aeg_common.cuh"
 
 #include <cuda.h>
@@ -50,11 +57,8 @@ __device__ unsigned int g_deverr_attn = 0;
 constexpr int kHeadDim = 128;
 constexpr int kHalves = kHeadDim / 64;  // 128-byte rows per (token, head)
 constexpr int kBlockTokens = 16;
-constexpr int kMaxTargetUnits = 8192;   // upper bound on the plan's balanced unit count
-constexpr int kMaxSplits = 64;          // splits of one (sequence, KV head) at most
-constexpr int kMinChunk = 4;            // blocks per unit at least (unless the sequence is shorter)
+constexpr int kMaxWarps = 4096;         // worker warps of one launch the workspace is sized for
 constexpr int kPlanThreads = 256;
-constexpr int kPlanBins = 1024;         // size classes of the longest-first unit order
 constexpr int kPlanCachedSeqs = 4096;   // sequences whose block counts the plan keeps in smem
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -65,44 +69,65 @@ constexpr int kBoxBytes = kHalves * kBlockTokens * 128;  // one (block, head) K 
 constexpr int kStageBytes = 2 * kBoxBytes;
 
 // Header words of the workspace.
-constexpr int kHdrUnits = 0, kHdrChunk = 1, kHdrPairs = 2, kHdrSplitPairs = 3, kHdrWork = 8, kHdrExit = 9;
+constexpr int kHdrItems = 0, kHdrWarps = 1, kHdrUnits = 2, kHdrSplitPairs = 3, kHdrSlots = 4,
+              kHdrMergeItems = 5, kHdrBar = 8, kHdrDone = 9;
+constexpr int kMergeBatch = 16;  // pieces a lane loads per round trip in the split merge
 
 // ---------------------------------------------------------------------------------------
 // Workspace layout (all offsets 256-byte aligned):
-//   header      : int32[64]  {num_units, chunk, num_pairs, num_split_pairs, .., work, exit}
-//   split_pairs : int4[P]    {pair, first unit, nsplit, 0} of every split (sequence, head)
-//   units       : int4[2 * max_units]  {pair, j0, j1, (split << 16) | nsplit},
+//   header      : int32[64]  {items, warps, units, split pairs, partial slots, .., barrier, done}
+//   warp_rec    : int4[3 * (max_warps + 1)]  per worker warp w: {first unit, 0, 0, 0} and a copy of
+//                            its first unit's record (one load starts a warp); entry `warps`
+//                            holds the end of the unit list
+//   split_pairs : int4[P]    {pair, first partial slot, nsplit, q} of every (sequence, head) cut
+//                            across warps (nsplit >= 2), and {pair, 0, 0, 1} of every empty one;
+//                            its merge is G * q items (query head, one of q dimension chunks)
+//   merge_rec   : int4[max_warps]  per warp: {split-pair entry, item within it, items, 0}, its
+//                            share of the merge items (balanced like the blocks)
+//   units       : int4[2 * max_units]  {pair, j0, j1, partial slot or -1},
 //                                      {seq_len, block id of items 0, 1, 2}
-//   part_ml     : float2[max_units * G]        (max in log2 units, sum) per query head
-//   part_o      : float [max_units * G * D]    partial outputs, scaled by 2^-max
+//   part_ml     : float2[max_slots * G]        (max in log2 units, sum) per query head
+//   part_o      : float [max_slots * G * D]    partial outputs, scaled by 2^-max
 struct WsLayout {
-  size_t split_pairs, units, part_ml, part_o, total;
-  int max_units;
+  size_t warp_rec, split_pairs, merge_rec, units, part_ml, part_o, total;
+  int max_warps, max_units, max_slots;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-WsLayout ws_layout(int B, int Hq, int Hkv, int D) {
+// Units: one per non-empty pair plus one per cut (a worker's range starting inside a pair), so
+// at most P + warps. Partial slots: only units of cut pairs have one, at most 2 * warps.
+WsLayout layout_for(int B, int Hq, int Hkv, int D, int max_warps) {
   WsLayout w{};
   const int G = Hq / Hkv;
   const int64_t P = int64_t(B) * Hkv;
-  w.max_units = static_cast<int>(kMaxTargetUnits + P);
+  w.max_warps = max_warps;
+  w.max_units = static_cast<int>(P + max_warps);
+  w.max_slots = 2 * max_warps;
   size_t off = 256;
+  w.warp_rec = off;
+  off = align256(off + 3 * sizeof(int4) * size_t(max_warps + 1));
   w.split_pairs = off;
   off = align256(off + sizeof(int4) * P);
+  w.merge_rec = off;
+  off = align256(off + sizeof(int4) * size_t(max_warps));
   w.units = off;
   off = align256(off + 2 * sizeof(int4) * size_t(w.max_units));
   w.part_ml = off;
-  off = align256(off + sizeof(float2) * size_t(w.max_units) * G);
+  off = align256(off + sizeof(float2) * size_t(w.max_slots) * G);
   w.part_o = off;
-  off = align256(off + sizeof(float) * size_t(w.max_units) * G * D);
+  off = align256(off + sizeof(float) * size_t(w.max_slots) * G * D);
   w.total = off;
   return w;
 }
 
+WsLayout ws_layout(int B, int Hq, int Hkv, int D) { return layout_for(B, Hq, Hkv, D, kMaxWarps); }
+
 struct WsPtrs {
   int* header;
+  int4* warp_rec;
   int4* split_pairs;
+  int4* merge_rec;
   int4* units;
   float2* part_ml;
   float* part_o;
@@ -110,13 +135,17 @@ struct WsPtrs {
 
 inline WsPtrs ws_ptrs(void* ws, const WsLayout& L) {
   char* b = static_cast<char*>(ws);
-  return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int4*>(b + L.split_pairs),
-                reinterpret_cast<int4*>(b + L.units), reinterpret_cast<float2*>(b + L.part_ml),
-                reinterpret_cast<float*>(b + L.part_o)};
+  return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int4*>(b + L.warp_rec),
+                reinterpret_cast<int4*>(b + L.split_pairs), reinterpret_cast<int4*>(b + L.merge_rec),
+                reinterpret_cast<int4*>(b + L.units),
+                reinterpret_cast<float2*>(b + L.part_ml), reinterpret_cast<float*>(b + L.part_o)};
 }
 
 // ---------------------------------------------------------------------------------------
-// Plan kernel (one CTA): chunk size, split counts, unit list, split-pair list.
+// Plan kernel (one CTA). The I (pair, block) items of the batch, in pair order, are cut into
+// Wp = min(W, I) contiguous ranges of equal size (up to one item), one per worker warp: worker
+// w < Wp starts at item floor(w * I / Wp), workers from Wp on get nothing. Units are the pieces
+// of pairs between pair ends and worker starts.
 
 __device__ __forceinline__ int seq_blocks(const int* seq_lens, int b, int cap, bool report) {
   int n = seq_lens[b];
@@ -127,19 +156,26 @@ __device__ __forceinline__ int seq_blocks(const int* seq_lens, int b, int cap, b
   return (n + kBlockTokens - 1) / kBlockTokens;
 }
 
-__device__ __forceinline__ int splits_for(int nb, int chunk) {
-  int ns = (nb + chunk - 1) / chunk;
-  ns = ns < 1 ? 1 : ns;
-  return ns > kMaxSplits ? kMaxSplits : ns;
+// First item of worker w. Products stay below 2^63: I <= kMaxItems and w, W <= kMaxWarps.
+constexpr long long kMaxItems = 1LL << 48;
+
+__device__ __forceinline__ long long worker_start(long long w, long long I, int W) { return w * I / W; }
+
+// Number of workers whose first item is <= x (worker 0 starts at item 0).
+__device__ __forceinline__ long long workers_le(long long x, long long I, int W) {
+  if (x < 0) return 0;
+  const long long c = ((x + 1) * W + I - 1) / I;
+  return c < W ? c : W;
 }
 
-__device__ __forceinline__ int size_bin(int nb, int chunk) {
-  if (chunk < kPlanBins) return nb;
-  const long long b = static_cast<long long>(nb) * (kPlanBins - 1) / chunk;
-  return static_cast<int>(b);
+// Dimension chunks of a pair's merge: enough that a lane loads at most kMergeBatch pieces.
+__device__ __forceinline__ int merge_chunks(int ns) {
+  int q = 1;
+  while (q < 32 && ns > q * kMergeBatch) q *= 2;
+  return q;
 }
 
-// Block-wide exclusive scan of one int per thread; also returns the total.
+// Block-wide exclusive scans of one value per thread; also return the total.
 __device__ __forceinline__ int block_excl_scan(int v, int* s_warp, int& total) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   int incl = v;
@@ -159,118 +195,157 @@ __device__ __forceinline__ int block_excl_scan(int v, int* s_warp, int& total) {
   return off + incl - v;
 }
 
-// Unit order, longest first: all units of split (sequence, head) pairs (each about `chunk`
-// blocks) in pair order, then the unsplit pairs by decreasing block count. Workers take units
-// in this order, so the tail of a launch is made of the smallest ones.
-__global__ void __launch_bounds__(kPlanThreads)
+__device__ __forceinline__ long long block_excl_scan64(long long v, long long* s_warp, long long& total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  long long incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  __syncthreads();
+  if (lane == 31) s_warp[wid] = incl;
+  __syncthreads();
+  long long off = 0;
+  total = 0;
+  for (int i = 0; i < kPlanThreads / 32; ++i) {
+    if (i < wid) off += s_warp[i];
+    total += s_warp[i];
+  }
+  return off + incl - v;
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
 decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tables, int B, int Hkv,
-                   int table_stride, int target_units, WsPtrs ws) {
+                   int G, int table_stride, int W, WsPtrs ws) {
   __shared__ long long s_red[kPlanThreads / 32];
   __shared__ int s_warp[kPlanThreads / 32];
-  __shared__ int s_hist[kPlanBins];
-  __shared__ int s_cursor[kPlanBins];
   __shared__ int s_nb[kPlanCachedSeqs];  // blocks per sequence (first kPlanCachedSeqs sequences)
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int tid = threadIdx.x;
   const int P = B * Hkv;
   const int cap = table_stride * kBlockTokens;
+  const int per = (P + kPlanThreads - 1) / kPlanThreads;
+  const int p0 = min(P, tid * per), p1 = min(P, p0 + per);
 
-  for (int i = tid; i < kPlanBins; i += kPlanThreads) s_hist[i] = 0;
-
-  // Pass 1: total (block, head) items -> chunk.
-  long long local = 0;
   for (int b = tid; b < B; b += kPlanThreads) {
     const int nb = seq_blocks(seq_lens, b, cap, true);
     if (b < kPlanCachedSeqs) s_nb[b] = nb;
-    local += nb;
   }
+  __syncthreads();
   auto blocks_of = [&](int b) { return b < kPlanCachedSeqs ? s_nb[b] : seq_blocks(seq_lens, b, cap, false); };
-  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-  if (lane == 0) s_red[wid] = local;
-  __syncthreads();
-  long long total = 0;
-  for (int i = 0; i < kPlanThreads / 32; ++i) total += s_red[i];
-  total *= Hkv;
-  int chunk = static_cast<int>((total + target_units - 1) / target_units);
-  chunk = chunk < kMinChunk ? kMinChunk : chunk;
 
-  // Pass 2: split units and split pairs counted over contiguous pair ranges; unsplit pairs binned.
-  const int per = (P + kPlanThreads - 1) / kPlanThreads;
-  const int p0 = min(P, tid * per), p1 = min(P, p0 + per);
-  int cnt_units = 0, cnt_pairs = 0;
-  for (int p = p0; p < p1; ++p) {
-    const int nb = blocks_of(p / Hkv);
-    const int ns = splits_for(nb, chunk);
-    if (ns > 1) {
-      cnt_units += ns;
-      ++cnt_pairs;
-    } else {
-      atomicAdd(&s_hist[size_bin(nb, chunk)], 1);
+  // Pass 1: items of this thread's pairs -> item offset of its first pair, total I.
+  long long local = 0;
+  for (int p = p0; p < p1; ++p) local += blocks_of(p / Hkv);
+  long long I = 0;
+  const long long o_t = block_excl_scan64(local, s_red, I);
+  if (I > kMaxItems) {  // beyond any pool this plan can address: plan nothing, report it
+    if (tid == 0) {
+      atomicOr(&g_deverr_attn, AEG_DEVERR_SEQ_LEN_RANGE);
+      ws.header[kHdrWarps] = W;
+      ws.header[kHdrUnits] = 0;
+      ws.header[kHdrSplitPairs] = 0;
+      ws.header[kHdrBar] = 0;
+      ws.header[kHdrDone] = 0;
     }
+    for (int w = tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(0, 0, 0, 0);
+    for (int w = tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(0, 0, 0, 0);
+    return;
   }
-  int n_split_units = 0, n_split_pairs = 0;
-  int u = block_excl_scan(cnt_units, s_warp, n_split_units);
-  int sp = block_excl_scan(cnt_pairs, s_warp, n_split_pairs);
-
-  // Descending-size offsets of the bins: thread t owns bins [4t, 4t + 4); the offset of its
-  // bins is the number of unsplit units in all higher bins (a reversed block scan).
-  static_assert(kPlanBins == 4 * kPlanThreads, "four bins per plan thread");
-  int loc[4], own = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    loc[i] = s_hist[4 * tid + i];
-    own += loc[i];
-  }
-  __syncthreads();
-  s_cursor[kPlanThreads - 1 - tid] = own;  // reversed order (scratch use of s_cursor)
-  __syncthreads();
-  int dummy = 0;
-  const int rexcl = block_excl_scan(s_cursor[tid], s_warp, dummy);
-  __syncthreads();
-  s_cursor[kPlanBins - 1 - tid] = rexcl;  // units owned by threads above (kPlanThreads - 1 - tid)
-  __syncthreads();
-  const int higher = s_cursor[kPlanBins - 1 - (kPlanThreads - 1 - tid)];
-  __syncthreads();
-  int run = n_split_units + higher;
-#pragma unroll
-  for (int i = 3; i >= 0; --i) {
-    s_cursor[4 * tid + i] = run;
-    run += loc[i];
-  }
-  if (tid == 0) {
-    ws.header[kHdrUnits] = run;  // thread 0 owns the lowest bins: its running end is the total
-    ws.header[kHdrChunk] = chunk;
-    ws.header[kHdrPairs] = P;
-    ws.header[kHdrSplitPairs] = n_split_pairs;
-    ws.header[kHdrWork] = 0;
-    ws.header[kHdrExit] = 0;
-  }
-  __syncthreads();
-
-  // Pass 3: write the units and the split-pair list. A unit record also carries the sequence
-  // length and its first three block ids, so that a worker can request its first tiles after
-  // one load.
-  auto put = [&](int idx, int p, int j0, int j1, int sw) {
-    const int b = p / Hkv;
-    const int* tb = tables + static_cast<int64_t>(b) * table_stride + j0;
-    const int n = j1 - j0;
-    const int n_ctx = min(max(seq_lens[b], 0), cap);
-    ws.units[2 * idx] = make_int4(p, j0, j1, sw);
-    ws.units[2 * idx + 1] = make_int4(n_ctx, n > 0 ? tb[0] : 0, n > 1 ? tb[1] : 0, n > 2 ? tb[2] : 0);
+  const int Wp = I < W ? static_cast<int>(I) : W;  // workers with items; their starts are distinct
+  auto cuts = [&](long long o, int nb) {  // workers starting strictly inside the pair's items
+    return static_cast<int>(workers_le(o + nb - 1, I, Wp) - workers_le(o, I, Wp));
   };
+
+  // Pass 2: units, split-pair entries, partial slots and merge items of this thread's pairs.
+  int n_units = 0, n_sp = 0, n_slots = 0;
+  long long n_mi = 0;
+  long long o = o_t;
   for (int p = p0; p < p1; ++p) {
     const int nb = blocks_of(p / Hkv);
-    const int ns = splits_for(nb, chunk);
-    if (ns > 1) {
-      ws.split_pairs[sp++] = make_int4(p, u, ns, 0);
-      for (int s = 0; s < ns; ++s) {
-        const int j0 = static_cast<int>((static_cast<long long>(s) * nb) / ns);
-        const int j1 = static_cast<int>((static_cast<long long>(s + 1) * nb) / ns);
-        put(u++, p, j0, j1, (s << 16) | ns);
-      }
-    } else {
-      const int pos = atomicAdd(&s_cursor[size_bin(nb, chunk)], 1);
-      put(pos, p, 0, nb, 1);
+    if (nb == 0) {
+      ++n_sp;
+      n_mi += G;
+      continue;
     }
+    const int c = cuts(o, nb);
+    n_units += c + 1;
+    if (c > 0) {
+      ++n_sp;
+      n_slots += c + 1;
+      n_mi += static_cast<long long>(G) * merge_chunks(c + 1);
+    }
+    o += nb;
+  }
+  int U = 0, S = 0, SL = 0;
+  int u = block_excl_scan(n_units, s_warp, U);
+  int sp = block_excl_scan(n_sp, s_warp, S);
+  int slot = block_excl_scan(n_slots, s_warp, SL);
+  long long MI = 0;
+  long long mo = block_excl_scan64(n_mi, s_red, MI);
+  const int Wm = MI < W ? static_cast<int>(MI) : W;  // warps with merge items
+  // Warps whose share of the merge items starts in [mo0, mo0 + n) get {entry, item within it,
+  // items}; warp w's share is [floor(w * MI / Wm), floor((w + 1) * MI / Wm)).
+  auto mark_merge = [&](int entry, long long mo0, int n) {
+    const long long w_hi = workers_le(mo0 + n - 1, MI, Wm);
+    for (long long w = workers_le(mo0 - 1, MI, Wm); w < w_hi; ++w) {
+      const long long st = worker_start(w, MI, Wm);
+      const long long en = w + 1 < Wm ? worker_start(w + 1, MI, Wm) : MI;
+      ws.merge_rec[w] = make_int4(entry, static_cast<int>(st - mo0), static_cast<int>(en - st), 0);
+    }
+  };
+  if (tid == 0) {
+    ws.header[kHdrItems] = static_cast<int>(I < 0x7fffffffLL ? I : 0x7fffffffLL);
+    ws.header[kHdrWarps] = W;
+    ws.header[kHdrUnits] = U;
+    ws.header[kHdrSplitPairs] = S;
+    ws.header[kHdrSlots] = SL;
+    ws.header[kHdrMergeItems] = static_cast<int>(MI < 0x7fffffffLL ? MI : 0x7fffffffLL);
+    ws.header[kHdrBar] = 0;
+    ws.header[kHdrDone] = 0;
+  }
+  for (int w = Wp + tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(U, 0, 0, 0);  // empty ranges
+  for (int w = Wm + tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(S, 0, 0, 0);      // no merge items
+
+  // Pass 3: write units, split-pair entries and the workers' first-unit records.
+  o = o_t;
+  for (int p = p0; p < p1; ++p) {
+    const int b = p / Hkv;
+    const int nb = blocks_of(b);
+    if (nb == 0) {
+      mark_merge(sp, mo, G);
+      mo += G;
+      ws.split_pairs[sp++] = make_int4(p, 0, 0, 1);
+      continue;
+    }
+    const int n_ctx = min(max(seq_lens[b], 0), cap);
+    const int* tb = tables + static_cast<int64_t>(b) * table_stride;
+    const int c = cuts(o, nb);
+    const long long wc = workers_le(o, I, Wp);  // first worker starting after item o
+    if (c > 0) {
+      const int q = merge_chunks(c + 1);
+      mark_merge(sp, mo, G * q);
+      mo += static_cast<long long>(G) * q;
+      ws.split_pairs[sp++] = make_int4(p, slot, c + 1, q);
+    }
+    for (int k = 0; k <= c; ++k) {
+      const long long xa = k == 0 ? o : worker_start(wc + k - 1, I, Wp);
+      const long long xb = k == c ? o + nb : worker_start(wc + k, I, Wp);
+      const int j0 = static_cast<int>(xa - o), j1 = static_cast<int>(xb - o);
+      const int n = j1 - j0;
+      const int4 ra = make_int4(p, j0, j1, c > 0 ? slot++ : -1);
+      const int4 rb = make_int4(n_ctx, tb[j0], n > 1 ? tb[j0 + 1] : 0, n > 2 ? tb[j0 + 2] : 0);
+      ws.units[2 * u] = ra;
+      ws.units[2 * u + 1] = rb;
+      // workers whose range starts at item xa begin with this unit
+      const long long w_hi = workers_le(xa, I, Wp);
+      for (long long w = workers_le(xa - 1, I, Wp); w < w_hi; ++w) {
+        ws.warp_rec[3 * w] = make_int4(u, 0, 0, 0);
+        ws.warp_rec[3 * w + 1] = ra;
+        ws.warp_rec[3 * w + 2] = rb;
+      }
+      ++u;
+    }
+    o += nb;
   }
 }
 
@@ -288,7 +363,9 @@ struct AttnParams {
   int G;
   int Hkv;
   int num_pairs;  // B * Hkv
-  int max_units;  // capacity of the workspace unit list
+  int max_warps;  // capacities of the workspace lists
+  int max_units;
+  int max_slots;
   int64_t num_blocks;
   float scale_log2;
   int q_bulk;  // query rows are 16-byte aligned: stage them with bulk copies
@@ -305,20 +382,141 @@ struct AttnParams {
   WsPtrs ws;
 };
 
-// A unit read from the workspace is used only if it is consistent with this call's shape; a
-// workspace that was not planned for this call (or not planned at all) is skipped and reported
-// instead of steering loads out of bounds.
-__device__ __forceinline__ bool unit_ok(const int4& un, const int4& un1, int u, const AttnParams& p) {
-  const int split = un.w >> 16, nsplit = un.w & 0xffff;
-  return un.x >= 0 && un.x < p.num_pairs && un.y >= 0 && un.y <= un.z && un.z <= p.table_stride && nsplit >= 1 &&
-         nsplit <= kMaxSplits && split < nsplit && u - split >= 0 && u - split + nsplit <= p.max_units &&
-         un1.x >= 0 && un1.x <= p.table_stride * kBlockTokens && un.z * kBlockTokens < un1.x + kBlockTokens;
+// Items (blocks) of a unit record, or 0 if the record is not consistent with this call's shape:
+// a workspace that was not planned for this call is skipped and reported instead of steering
+// loads out of bounds.
+__device__ __forceinline__ int unit_items(const int4& a, const int4& b, const AttnParams& p) {
+  const bool ok = a.x >= 0 && a.x < p.num_pairs && a.y >= 0 && a.y < a.z && a.z <= p.table_stride && a.w >= -1 &&
+                  a.w < p.max_slots && b.x >= 0 && b.x <= p.table_stride * kBlockTokens &&
+                  a.z * kBlockTokens < b.x + kBlockTokens;
+  return ok ? a.z - a.y : 0;
+}
+
+__device__ __forceinline__ int4 shfl4(const int4& v, int src) {
+  return make_int4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                   __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
 }
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float2 ld_cg_f2(const float2* ptr) {
+  float2 r;
+  asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(ptr));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
+  float4 r;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  return r;
+}
+
+// Split merge of one item = (cut pair, query head n, dimension chunk `chunk` of q), one warp:
+// lane = (piece group g, float4 column c) with 32 / q columns per chunk; group g takes pieces
+// g, g + q, g + 2q, ... and folds them in with a running maximum (each piece's max, sum and row
+// chunk arrive in the same round trip), then the q groups are combined by xor shuffles. An
+// empty pair (ns = 0) gets a zero row. Partials are read through L2 (ld.global.cg): other SMs
+// wrote them.
+template <typename T>
+__device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, int n, int chunk, int lane) {
+  const int G = p.G;
+  const int q = e.w, ns = e.z;
+  const int lq = __ffs(q) - 1;       // q is a power of two
+  const int lc = 5 - lq;             // log2 of the float4 columns per chunk
+  const int c = lane & ((1 << lc) - 1), g = lane >> lc;
+  const int col = (chunk << lc) + c;  // float4 column of the 128-dim row
+  const float4* po4 = reinterpret_cast<const float4*>(p.ws.part_o);
+  float M = -INFINITY, L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = g; s0 < ns; s0 += q * kMergeBatch) {
+    float2 ml[kMergeBatch];
+    float4 v[kMergeBatch];
+    // All loads of the batch are issued before any of them is used (ordered volatile loads):
+    // the batch costs one round trip. Both loops stop at the lane's last piece, so a short
+    // merge executes only the instructions of its pieces.
+    const int cnt = min(kMergeBatch, (ns - s0 + q - 1) >> lq);
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      if (i >= cnt) break;
+      const int64_t row = static_cast<int64_t>(e.y + s0 + (i << lq)) * G + n;
+      ml[i] = ld_cg_f2(&p.ws.part_ml[row]);
+      v[i] = ld_cg_f4(po4 + row * (kHeadDim / 4) + col);
+    }
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      if (i >= cnt) break;
+      if (ml[i].x != -INFINITY) {
+        const float Mn = fmaxf(M, ml[i].x);
+        const float r = M != -INFINITY ? ex2(M - Mn) : 0.f;
+        const float w = ex2(ml[i].x - Mn);
+        acc.x = acc.x * r + w * v[i].x;
+        acc.y = acc.y * r + w * v[i].y;
+        acc.z = acc.z * r + w * v[i].z;
+        acc.w = acc.w * r + w * v[i].w;
+        L = L * r + w * ml[i].y;
+        M = Mn;
+      }
+    }
+  }
+  for (int off = 1 << lc; off < 32; off <<= 1) {
+    const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
+    const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
+    float4 ao;
+    ao.x = __shfl_xor_sync(0xffffffffu, acc.x, off);
+    ao.y = __shfl_xor_sync(0xffffffffu, acc.y, off);
+    ao.z = __shfl_xor_sync(0xffffffffu, acc.z, off);
+    ao.w = __shfl_xor_sync(0xffffffffu, acc.w, off);
+    const float Mn = fmaxf(M, Mo);
+    const float r1 = M != -INFINITY ? ex2(M - Mn) : 0.f;
+    const float r2 = Mo != -INFINITY ? ex2(Mo - Mn) : 0.f;
+    acc.x = acc.x * r1 + ao.x * r2;
+    acc.y = acc.y * r1 + ao.y * r2;
+    acc.z = acc.z * r1 + ao.z * r2;
+    acc.w = acc.w * r1 + ao.w * r2;
+    L = L * r1 + Lo * r2;
+    M = Mn;
+  }
+  if (g == 0) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int b = e.x / p.Hkv, h = e.x % p.Hkv;
+    T* dst = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+             (static_cast<int64_t>(h) * G + n) * kHeadDim + col * 4;
+    if (aligned(dst, 8)) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(acc.x * inv, acc.y * inv), pack2<T>(acc.z * inv, acc.w * inv));
+    } else {
+      dst[0] = from_float<T>(acc.x * inv);
+      dst[1] = from_float<T>(acc.y * inv);
+      dst[2] = from_float<T>(acc.z * inv);
+      dst[3] = from_float<T>(acc.w * inv);
+    }
+  }
+}
+
+// A split-pair entry is used only if it fits this call's shape (see unit_items).
+__device__ __forceinline__ bool entry_ok(const int4& e, const AttnParams& p) {
+  const int q = e.w;
+  const bool q_ok = q == 1 || q == 2 || q == 4 || q == 8 || q == 16 || q == 32;
+  return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.z >= 0 && e.y + e.z <= p.max_slots && q_ok;
+}
+
+// Waits until *ctr >= target (the grid's arrival count), for at most kWaitLimitNs.
+__device__ __forceinline__ bool grid_wait(const int* ctr, int target) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_gpu(ctr) < target) {
+    __nanosleep(64);
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
 }
 
 template <int NT>
@@ -331,30 +529,6 @@ struct AttnSmem {
   static constexpr size_t kDynamic = size_t(kTotal) + 1024;  // + alignment slack
   static_assert(kPerWarp % 1024 == 0, "per-warp regions must keep 1024-byte alignment");
 };
-
-// One work unit as a warp sees it (all lanes hold the same values, except `tbl`, `knew`, `vnew`).
-struct Unit {
-  int u;        // unit index, -1 = none (queue exhausted)
-  int b, h, j0, n, split, nsplit, n_ctx;
-  int tbl;      // this lane's block id of the table chunk starting at item `tbase`
-  int tbase;
-  int issued;   // items whose tiles were requested
-  int bf0, bf1, bf2;  // block ids of items 0..2 (from the unit record)
-  int blk_last; // block id of the last item (fused cache write)
-  int last;     // the unit holds the sequence's newest token (fused cache write)
-  uint2 knew;   // this lane's 4 elements of the new K / V row of head h (fused cache write)
-  uint2 vnew;
-};
-
-__device__ __forceinline__ void unit_clear(Unit& x) {
-  x.u = -1;
-  x.b = x.h = x.j0 = x.n = x.split = x.n_ctx = 0;
-  x.nsplit = 1;
-  x.tbl = x.tbase = x.issued = 0;
-  x.bf0 = x.bf1 = x.bf2 = x.blk_last = 0;
-  x.last = 0;
-  x.knew = x.vnew = make_uint2(0u, 0u);
-}
 
 template <typename T, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -390,9 +564,10 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   pdl_wait_primary();
   pdl_launch_dependents();
 
-  const int num_units = min(max(p.ws.header[kHdrUnits], 0), p.max_units);
   const int G = p.G;
   const int Hkv = p.Hkv;
+  const int gw = static_cast<int>(blockIdx.x) * kWarps + warp;
+  const int total_warps = static_cast<int>(gridDim.x) * kWarps;
   const uint64_t pol = l2_policy_evict_first();
   const T* q = static_cast<const T*>(p.q);
   T* out = static_cast<T*>(p.out);
@@ -410,71 +585,70 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
   };
 
-  // Unit fetch in three phases so that its latency overlaps the processing of blocks:
-  // A) reserve a unit index, B) load its record, C) unpack it, load the table chunk (and the
-  // new K/V row for the fused write) and start the bulk copy of its query rows.
-  // The first unit of every warp is its global warp index; later ones come from the counter.
-  const int total_warps = static_cast<int>(gridDim.x) * kWarps;
-  bool first_fetch = true;
-  auto phase_a = [&]() -> int {
-    int u = 0;
-    if (first_fetch) {
-      u = static_cast<int>(blockIdx.x) * kWarps + warp;
-      first_fetch = false;
-    } else if (lane == 0) {
-      u = total_warps + atomicAdd(&p.ws.header[kHdrWork], 1);
+  // This worker's unit range and its first unit record, in one round trip.
+  int4 r0 = make_int4(0, 0, 0, 0);
+  if (lane < 3)
+    r0 = p.ws.warp_rec[3 * gw + lane];
+  else if (lane == 3)
+    r0.x = p.ws.warp_rec[3 * (gw + 1)].x;
+  else if (lane == 4)
+    r0.x = p.ws.header[kHdrWarps];
+  else if (lane == 5)
+    r0.x = p.ws.header[kHdrUnits];
+  else if (lane == 6)
+    r0.x = p.ws.header[kHdrSplitPairs];
+  else if (lane == 7)
+    r0 = p.ws.merge_rec[gw];
+  const int u_beg = __shfl_sync(0xffffffffu, r0.x, 0);
+  const int u_end = __shfl_sync(0xffffffffu, r0.x, 3);
+  const int planned_warps = __shfl_sync(0xffffffffu, r0.x, 4);
+  const int planned_units = __shfl_sync(0xffffffffu, r0.x, 5);
+  const int n_entries = min(max(__shfl_sync(0xffffffffu, r0.x, 6), 0), p.num_pairs);
+  const int4 mr = shfl4(r0, 7);  // this warp's share of the split merge
+  int n_units = u_end - u_beg;
+  if (!(planned_warps == total_warps && planned_units <= p.max_units && u_beg >= 0 && u_beg <= u_end &&
+        u_end <= planned_units)) {
+    if (lane == 0 && n_units != 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
+    n_units = 0;
+  }
+
+  // Unit records, one per lane: lane (k % 32) holds the record of the worker's unit k for the
+  // 32 units from the one being computed on; each finished unit's lane loads the unit 32 ahead.
+  // Unit 0 is also kept in fa/fb, so that starting it does not wait for the other lanes' loads.
+  const int4 fa = shfl4(r0, 1), fb = shfl4(r0, 2);
+  int4 ra = fa, rb = fb;
+  if (lane > 0) {
+    if (lane < n_units) {
+      ra = p.ws.units[2 * (u_beg + lane)];
+      rb = p.ws.units[2 * (u_beg + lane) + 1];
+    } else {
+      ra = make_int4(0, 0, 0, -1);
+      rb = make_int4(0, 0, 0, 0);
     }
-    return u;
+  }
+
+  // Query rows of unit k into the query slot (completes on qbar). A unit whose record is not
+  // usable still completes the phase, so that the consumer's phases stay in step.
+  auto rec = [&](int k, int4& a, int4& bb) {
+    if (k == 0) {
+      a = fa;
+      bb = fb;
+    } else {
+      a = shfl4(ra, k & 31);
+      bb = shfl4(rb, k & 31);
+    }
   };
-  auto phase_b = [&](int u_raw, int4& un1) -> int4 {
-    const int u = __shfl_sync(0xffffffffu, u_raw, 0);
-    if (u >= num_units) {
-      un1 = make_int4(0, 0, 0, 0);
-      return make_int4(-1, u, 0, 0);
-    }
-    un1 = p.ws.units[2 * u + 1];
-    return p.ws.units[2 * u];
-  };
-  auto phase_c = [&](int u_raw, const int4& un, const int4& un1, Unit& x) -> bool {  // false: invalid, refetch
-    const int u = __shfl_sync(0xffffffffu, u_raw, 0);
-    unit_clear(x);
-    if (u >= num_units) return true;  // x.u = -1: nothing left
-    if (!unit_ok(un, un1, u, p)) {
-      if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
-      return false;
-    }
-    x.u = u;
-    x.b = un.x / Hkv;
-    x.h = un.x % Hkv;
-    x.j0 = un.y;
-    x.n = un.z - un.y;
-    x.split = un.w >> 16;
-    x.nsplit = un.w & 0xffff;
-    x.n_ctx = un1.x;
-    x.bf0 = un1.y;
-    x.bf1 = un1.z;
-    x.bf2 = un1.w;
-    // table chunk for items 3 .. 34 (items 0..2 come with the record)
-    const int* tb = p.tables + static_cast<int64_t>(x.b) * p.table_stride + x.j0 + 3;
-    x.tbase = 3;
-    x.tbl = lane < min(32, x.n - 3) ? tb[lane] : 0;
-    if (p.fuse_write && x.n > 0 && x.n_ctx > 0 && x.j0 + x.n == (x.n_ctx + kBlockTokens - 1) / kBlockTokens) {
-      // This unit reads the block of position n_ctx - 1: keep the new K/V row of head h to
-      // store it in the cache and patch it into the tile when that block is processed.
-      x.last = 1;
-      const uint32_t* kn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.k_new) +
-                                                             static_cast<int64_t>(x.b) * p.k_new_stride +
-                                                             static_cast<int64_t>(x.h) * kHeadDim) + 2 * lane;
-      const uint32_t* vn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.v_new) +
-                                                             static_cast<int64_t>(x.b) * p.v_new_stride +
-                                                             static_cast<int64_t>(x.h) * kHeadDim) + 2 * lane;
-      x.knew = make_uint2(kn[0], kn[1]);
-      x.vnew = make_uint2(vn[0], vn[1]);
-    }
-    // query rows of this unit into the (now free) query slot
-    const T* qsrc = q + static_cast<int64_t>(x.b) * p.q_stride + static_cast<int64_t>(x.h) * G * kHeadDim;
-    const uint32_t qbytes = G * kHeadDim * 2;
+  auto load_q = [&](int k) {
+    int4 a, bb;
+    rec(k, a, bb);
     fence_proxy_async_smem();
+    if (unit_items(a, bb, p) == 0) {
+      if (lane == 0) mbar_arrive(qbar);
+      return;
+    }
+    const int b = a.x / Hkv, h = a.x % Hkv;
+    const T* qsrc = q + static_cast<int64_t>(b) * p.q_stride + static_cast<int64_t>(h) * G * kHeadDim;
+    const uint32_t qbytes = G * kHeadDim * 2;
     if (p.q_bulk) {
       if (lane == 0) {
         mbar_arrive_expect_tx(qbar, qbytes);
@@ -486,55 +660,86 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(qbar);
     }
-    return true;
-  };
-  auto fetch_now = [&](Unit& x) {
-    while (true) {
-      const int ur = phase_a();
-      int4 un1;
-      const int4 un = phase_b(ur, un1);
-      if (phase_c(ur, un, un1, x)) return;
-    }
   };
 
-  // Requests the next tile of unit x into the ring.
-  auto issue = [&](Unit& x) {
-    const int k = x.issued;
+  // Issue walker: requests the tiles of the worker's units in order, kStages ahead of the
+  // consumer. Items 0..2 of a unit come with its record; later ones from a 32-entry chunk of
+  // the block table loaded when the walker enters the unit.
+  int ik = -1, ii = 0, in_ = 0, ih = 0, ibf0 = 0, ibf1 = 0, ibf2 = 0, itbase = 0, itbl = 0;
+  const int* itab = p.tables;
+  int sblk[kStages];  // block id of the tile in each stage (fused cache write)
+#pragma unroll
+  for (int i = 0; i < kStages; ++i) sblk[i] = 0;
+  auto issue_enter = [&](int k) {
+    ik = k;
+    ii = 0;
+    in_ = 0;
+    if (k >= n_units) return;
+    int4 a, bb;
+    rec(k, a, bb);
+    in_ = unit_items(a, bb, p);
+    if (in_ == 0) return;
+    ih = a.x % Hkv;
+    ibf0 = bb.y;
+    ibf1 = bb.z;
+    ibf2 = bb.w;
+    itab = p.tables + static_cast<int64_t>(a.x / Hkv) * p.table_stride + a.y;
+    itbase = 3;
+    itbl = (in_ > 3 && lane < min(32, in_ - 3)) ? itab[3 + lane] : 0;
+  };
+  auto issue_one = [&]() -> bool {
+    while (ik < n_units && ii >= in_) issue_enter(ik + 1);
+    if (ik >= n_units) return false;
     int blk;
-    if (k < 3) {
-      blk = k == 0 ? x.bf0 : (k == 1 ? x.bf1 : x.bf2);
+    if (ii < 3) {
+      blk = ii == 0 ? ibf0 : (ii == 1 ? ibf1 : ibf2);
     } else {
-      if (k - x.tbase >= 32) {
-        x.tbase = k;
-        const int* tb = p.tables + static_cast<int64_t>(x.b) * p.table_stride + x.j0 + k;
-        x.tbl = lane < min(32, x.n - k) ? tb[lane] : 0;
+      if (ii - itbase >= 32) {
+        itbase = ii;
+        itbl = lane < min(32, in_ - ii) ? itab[ii + lane] : 0;
       }
-      blk = __shfl_sync(0xffffffffu, x.tbl, k - x.tbase);
+      blk = __shfl_sync(0xffffffffu, itbl, ii - itbase);
     }
-    if (k == x.n - 1) x.blk_last = blk;
+    const uint32_t st = g_iss % kStages;
+#pragma unroll
+    for (int i = 0; i < kStages; ++i)
+      if (i == static_cast<int>(st)) sblk[i] = blk;
     fence_proxy_async_smem();  // the stage being refilled was read through the generic proxy
     if (lane == 0) {
       if (static_cast<unsigned long long>(static_cast<long long>(blk)) >= static_cast<unsigned long long>(p.num_blocks))
         atomicOr(&g_deverr_attn, AEG_DEVERR_BLOCK_ID_RANGE);  // TMA zero-fills it
       if (!abort) {
-        const uint32_t st = g_iss % kStages;
         uint8_t* dst = ring + st * kStageBytes;
         mbar_arrive_expect_tx(&full[st], kStageBytes);
-        tma_load_5d(dst, &kmap, &full[st], 0, 0, 0, x.h, blk, pol);
-        tma_load_5d(dst + kBoxBytes, &vmap, &full[st], 0, 0, 0, x.h, blk, pol);
+        tma_load_5d(dst, &kmap, &full[st], 0, 0, 0, ih, blk, pol);
+        tma_load_5d(dst + kBoxBytes, &vmap, &full[st], 0, 0, 0, ih, blk, pol);
       }
     }
     ++g_iss;
-    ++x.issued;
+    ++ii;
+    return true;
+  };
+  auto refill = [&]() {
+    while (g_iss - g_con < kStages && issue_one()) {
+    }
   };
 
-  Unit cur, nxt;
-  unit_clear(nxt);
-  fetch_now(cur);
-  while (cur.u >= 0 && cur.issued < cur.n && g_iss - g_con < kStages) issue(cur);
+  if (n_units > 0) load_q(0);
+  refill();
 
-  while (cur.u >= 0) {
-    // Query fragments (B operand of S^T = K Q^T) from the query slot.
+  for (int c = 0; c < n_units; ++c) {
+    if (c > 0 && lane == ((c - 1) & 31) && c + 31 < n_units) {
+      ra = p.ws.units[2 * (u_beg + c + 31)];
+      rb = p.ws.units[2 * (u_beg + c + 31) + 1];
+    }
+    int4 ua, ub;
+    rec(c, ua, ub);
+    const int n = unit_items(ua, ub, p);
+    if (n == 0 && lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
+    const int b = ua.x / Hkv, h = ua.x % Hkv, j0 = ua.y, slot = ua.w, n_ctx = ub.x;
+
+    // Query fragments (B operand of S^T = K Q^T) from the query slot; then the slot is free for
+    // the next unit's rows.
     if (!abort && !mbar_wait_bounded(qbar, q_phase, kWaitLimitNs)) report_timeout();
     q_phase ^= 1;
     uint32_t qf[NT][8][2];
@@ -550,6 +755,22 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       }
     }
     __syncwarp();
+    if (c + 1 < n_units) load_q(c + 1);
+    if (n == 0) continue;
+
+    // Fused cache write: this unit reads the block of position n_ctx - 1.
+    const bool last = p.fuse_write && n_ctx > 0 && j0 + n == (n_ctx + kBlockTokens - 1) / kBlockTokens;
+    uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
+    if (last) {
+      const uint32_t* kn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.k_new) +
+                                                             static_cast<int64_t>(b) * p.k_new_stride +
+                                                             static_cast<int64_t>(h) * kHeadDim) + 2 * lane;
+      const uint32_t* vn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.v_new) +
+                                                             static_cast<int64_t>(b) * p.v_new_stride +
+                                                             static_cast<int64_t>(h) * kHeadDim) + 2 * lane;
+      knew = make_uint2(kn[0], kn[1]);
+      vnew = make_uint2(vn[0], vn[1]);
+    }
 
     float o[8][NT][4];
     float m[NT][2], l[NT][2];
@@ -561,59 +782,34 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       for (int mt = 0; mt < 8; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
     }
 
-    // Prefetch state of the next unit.
-    int pf = 0, nxt_raw = 0;
-    int4 nxt_un = make_int4(0, 0, 0, 0), nxt_un1 = make_int4(0, 0, 0, 0);
-    bool nxt_ready = false;
-    auto prefetch_step = [&]() {
-      if (pf == 0) {
-        nxt_raw = phase_a();
-      } else if (pf == 1) {
-        nxt_un = phase_b(nxt_raw, nxt_un1);
-      } else if (pf == 2) {
-        if (phase_c(nxt_raw, nxt_un, nxt_un1, nxt)) {
-          nxt_ready = true;
-        } else {
-          pf = -1;  // invalid unit: start over (reported already)
-        }
-      }
-      if (pf < 3) ++pf;
-    };
-    auto refill = [&]() {
-      while (g_iss - g_con < kStages) {
-        if (cur.issued < cur.n)
-          issue(cur);
-        else if (nxt_ready && nxt.u >= 0 && nxt.issued < nxt.n)
-          issue(nxt);
-        else
-          break;
-      }
-    };
-
-    for (int k = 0; k < cur.n; ++k) {
+    for (int k = 0; k < n; ++k) {
       const uint32_t st = g_con % kStages, ph = (g_con / kStages) & 1;
       if (!abort && !mbar_wait_bounded(&full[st], ph, kWaitLimitNs)) report_timeout();
-      const int j = cur.j0 + k;
-      const int nvalid = min(kBlockTokens, cur.n_ctx - j * kBlockTokens);
+      const int j = j0 + k;
+      const int nvalid = min(kBlockTokens, n_ctx - j * kBlockTokens);
       if (!abort && nvalid > 0) {
         const uint32_t kbase = smem_u32(ring + st * kStageBytes);
         const uint32_t vbase = kbase + kBoxBytes;
-        if (cur.last && k == cur.n - 1) {
+        if (last && k == n - 1) {
           // Fused cache write: store the newest token's K/V row of head h in the cache (no other
           // reader of that row in this launch: other warps read other heads' rows) and patch it
           // into the swizzled tiles, which were fetched before the store.
-          const int t = (cur.n_ctx - 1) % kBlockTokens;
-          if (static_cast<unsigned long long>(static_cast<long long>(cur.blk_last)) <
+          int blk = 0;
+#pragma unroll
+          for (int i = 0; i < kStages; ++i)
+            if (i == static_cast<int>(st)) blk = sblk[i];
+          const int t = (n_ctx - 1) % kBlockTokens;
+          if (static_cast<unsigned long long>(static_cast<long long>(blk)) <
               static_cast<unsigned long long>(p.num_blocks)) {
-            const int64_t off = static_cast<int64_t>(cur.blk_last) * p.block_stride +
-                                (static_cast<int64_t>(t) * Hkv + cur.h) * kHeadDim + 4 * lane;
-            *reinterpret_cast<uint2*>(static_cast<T*>(p.k_cache) + off) = cur.knew;
-            *reinterpret_cast<uint2*>(static_cast<T*>(p.v_cache) + off) = cur.vnew;
+            const int64_t off = static_cast<int64_t>(blk) * p.block_stride +
+                                (static_cast<int64_t>(t) * Hkv + h) * kHeadDim + 4 * lane;
+            *reinterpret_cast<uint2*>(static_cast<T*>(p.k_cache) + off) = knew;
+            *reinterpret_cast<uint2*>(static_cast<T*>(p.v_cache) + off) = vnew;
           }
           const int half = lane >> 4, ch = (lane & 15) >> 1;
           const uint32_t soff = (half * kBlockTokens + t) * 128 + ((ch ^ (t & 7)) << 4) + (lane & 1) * 8;
-          *reinterpret_cast<uint2*>(ring + st * kStageBytes + soff) = cur.knew;
-          *reinterpret_cast<uint2*>(ring + st * kStageBytes + kBoxBytes + soff) = cur.vnew;
+          *reinterpret_cast<uint2*>(ring + st * kStageBytes + soff) = knew;
+          *reinterpret_cast<uint2*>(ring + st * kStageBytes + kBoxBytes + soff) = vnew;
           __syncwarp();
         }
 
@@ -624,8 +820,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const int tok = lr + ((lm & 1) << 3);
-          const int c = ks * 2 + (lm >> 1);
-          const uint32_t addr = kbase + ((c >> 3) * kBlockTokens + tok) * 128 + (((c & 7) ^ lr) << 4);
+          const int cc = ks * 2 + (lm >> 1);
+          const uint32_t addr = kbase + ((cc >> 3) * kBlockTokens + tok) * 128 + (((cc & 7) ^ lr) << 4);
           uint32_t a[4];
           ldmatrix_x4(a, addr);
 #pragma unroll
@@ -677,8 +873,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int tok = lr + ((lm >> 1) << 3);
-          const int c = mt * 2 + (lm & 1);
-          const uint32_t addr = vbase + ((c >> 3) * kBlockTokens + tok) * 128 + (((c & 7) ^ lr) << 4);
+          const int cc = mt * 2 + (lm & 1);
+          const uint32_t addr = vbase + ((cc >> 3) * kBlockTokens + tok) * 128 + (((cc & 7) ^ lr) << 4);
           uint32_t a[4];
           ldmatrix_x4_trans(a, addr);
 #pragma unroll
@@ -690,11 +886,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       }
       __syncwarp();
       ++g_con;
-      prefetch_step();
       refill();
     }
-    while (pf < 3) prefetch_step();
-    refill();
 
     // ---- unit result ----
 #pragma unroll
@@ -704,8 +897,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         l[nt][0] += __shfl_xor_sync(0xffffffffu, l[nt][0], off);
         l[nt][1] += __shfl_xor_sync(0xffffffffu, l[nt][1], off);
       }
-    if (cur.nsplit == 1) {
-      T* ob = out + static_cast<int64_t>(cur.b) * p.out_stride + static_cast<int64_t>(cur.h) * G * kHeadDim;
+    if (slot < 0) {
+      T* ob = out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(h) * G * kHeadDim;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int h0 = nt * 8 + 2 * quad;
@@ -725,7 +918,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         }
       }
     } else {
-      const int64_t base = static_cast<int64_t>(cur.u) * G;
+      const int64_t base = static_cast<int64_t>(slot) * G;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int h0 = nt * 8 + 2 * quad;
@@ -749,93 +942,56 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         }
       }
     }
-
-    cur = nxt;
-    unit_clear(nxt);
-    refill();
   }
 
-  // The last warp of the grid to finish resets the work counters for the next launch.
-  if (lane == 0) {
-    __threadfence();
-    const int done = atomicAdd(&p.ws.header[kHdrExit], 1);
-    if (done == total_warps - 1) {
-      p.ws.header[kHdrWork] = 0;
-      p.ws.header[kHdrExit] = 0;
+  // The first split-pair entry of this warp's merge share (plan data, read before the barrier).
+  int entry = mr.x, k = mr.y;
+  const bool share_ok = mr.z >= 0 && entry >= 0 && entry <= n_entries;
+  int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1);
+
+  // Grid-wide barrier, then the split merge. Every thread publishes its partials (fence); the
+  // CTA's warps meet at a CTA barrier and one thread per CTA arrives at the grid counter and
+  // waits for all CTAs. The grid is launched cooperatively (all CTAs resident), and the wait is
+  // bounded all the same.
+  __shared__ int s_go;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ctas = static_cast<int>(gridDim.x);
+    int go = 1;
+    const int arrived = atomicAdd(&p.ws.header[kHdrBar], 1) + 1;
+    if (arrived < ctas && !grid_wait(&p.ws.header[kHdrBar], ctas)) {
+      go = 0;
+      atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
     }
+    s_go = go;
   }
-}
-
-// ---------------------------------------------------------------------------------------
-// Combine kernel: merges the partials of every split (sequence, KV head). Work item =
-// (split pair, query head n of its group), one warp each, no block-level synchronisation:
-// lane c owns float4 column c of the 128-dim row and loads that column of kCombineBatch splits
-// at a time in the same round trip as the splits' (max, sum) pairs; the weights 2^(m_s - M) / L
-// are exchanged by shuffles.
-
-constexpr int kCombineThreads = 128;
-constexpr int kCombineWarps = kCombineThreads / 32;
-constexpr int kCombineBatch = 32;
-
-template <typename T>
-__global__ void __launch_bounds__(kCombineThreads)
-decode_combine_kernel(void* out_v, int64_t out_stride, int G, int Hkv, WsPtrs ws) {
-  T* out = static_cast<T*>(out_v);
-  const int lane = threadIdx.x & 31;
-  const int gw = static_cast<int>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
-  const int n_warps = static_cast<int>(gridDim.x) * kCombineWarps;
-  // The split-pair list comes from the plan kernel, which finished before the attention launch
-  // this kernel depends on started; it is read before waiting for the attention results.
-  const int n_items = ws.header[kHdrSplitPairs] * G;
-  int4 sp = gw < n_items ? ws.split_pairs[gw / G] : make_int4(0, 0, 0, 0);
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  const float4* po4 = reinterpret_cast<const float4*>(ws.part_o);
-  for (int item = gw; item < n_items; item += n_warps) {
-    const int n = item % G;
-    const int ns = min(sp.z, kMaxSplits);
-    const int64_t row0 = static_cast<int64_t>(sp.y) * G + n;  // partial row of split 0
-    const float2 a = lane < ns ? __ldcg(&ws.part_ml[row0 + static_cast<int64_t>(lane) * G]) : make_float2(-INFINITY, 0.f);
-    const float2 c = lane + 32 < ns ? __ldcg(&ws.part_ml[row0 + static_cast<int64_t>(lane + 32) * G])
-                                    : make_float2(-INFINITY, 0.f);
-    float4 v[kCombineBatch];
-#pragma unroll
-    for (int i = 0; i < kCombineBatch; ++i)
-      v[i] = i < ns ? __ldcg(po4 + (row0 + static_cast<int64_t>(i) * G) * (kHeadDim / 4) + lane)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    float M = fmaxf(a.x, c.x);
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    const float w = (M != -INFINITY && a.x != -INFINITY) ? ex2(a.x - M) : 0.f;
-    const float w2 = (M != -INFINITY && c.x != -INFINITY) ? ex2(c.x - M) : 0.f;
-    float L = w * a.y + w2 * c.y;
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < ns; s0 += kCombineBatch) {
-      if (s0 > 0) {
-#pragma unroll
-        for (int i = 0; i < kCombineBatch; ++i)
-          v[i] = s0 + i < ns ? __ldcg(po4 + (row0 + static_cast<int64_t>(s0 + i) * G) * (kHeadDim / 4) + lane)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  if (s_go && share_ok) {
+    for (int left = mr.z; left > 0; --left) {
+      if (k >= G * me.w) {  // next split-pair entry
+        ++entry;
+        k = 0;
+        me = entry < n_entries ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1);
       }
-#pragma unroll
-      for (int i = 0; i < kCombineBatch; ++i) {
-        const float wi = __shfl_sync(0xffffffffu, s0 + i < 32 ? w : w2, (s0 + i) & 31);
-        if (s0 + i < ns) {
-          acc.x += wi * v[i].x;
-          acc.y += wi * v[i].y;
-          acc.z += wi * v[i].z;
-          acc.w += wi * v[i].w;
-        }
+      if (!entry_ok(me, p) || k < 0) {
+        if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
+        break;
       }
+      merge_item<T>(p, me, k / me.w, k % me.w, lane);
+      ++k;
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int b = sp.x / Hkv, h = sp.x % Hkv;
-    T* dst = out + static_cast<int64_t>(b) * out_stride + (static_cast<int64_t>(h) * G + n) * kHeadDim + lane * 4;
-    dst[0] = from_float<T>(acc.x * inv);
-    dst[1] = from_float<T>(acc.y * inv);
-    dst[2] = from_float<T>(acc.z * inv);
-    dst[3] = from_float<T>(acc.w * inv);
-    if (item + n_warps < n_items) sp = ws.split_pairs[(item + n_warps) / G];
+  } else if (!share_ok && lane == 0) {
+    atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
+  }
+  // The last CTA to finish resets the barrier for the next launch with this plan.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(&p.ws.header[kHdrDone], 1);
+    if (done == static_cast<int>(gridDim.x) - 1) {
+      p.ws.header[kHdrBar] = 0;
+      p.ws.header[kHdrDone] = 0;
+    }
   }
 }
 
@@ -916,25 +1072,29 @@ int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams
     (void)cudaGetLastError();
     return set_error(AEG_ERR_CUDA, "decode attention kernel cannot be configured on this device");
   }
-  cudaLaunchAttribute attr[1] = {pdl_attr()};
+  if (num_sms() * per_sm * kWarps > prm.max_warps)
+    return set_error(AEG_ERR_UNSUPPORTED, "decode: %d worker warps exceed the workspace's %d", num_sms() * per_sm * kWarps,
+                     prm.max_warps);
+  // Cooperative: the kernel ends with a grid-wide barrier, so all of its CTAs must be resident.
+  cudaLaunchAttribute attr[2] = {pdl_attr(), {}};
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms() * per_sm));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = AttnSmem<NT>::kDynamic;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, NT>, km, vm, prm));
-
-  cudaLaunchConfig_t cc{};
-  cc.gridDim = dim3(static_cast<unsigned>(num_sms() * 4));
-  cc.blockDim = dim3(kCombineThreads);
-  cc.dynamicSmemBytes = 0;
-  cc.stream = stream;
-  cc.attrs = attr;
-  cc.numAttrs = 1;
-  AEG_CHECK_CUDA(cudaLaunchKernelEx(&cc, decode_combine_kernel<T>, prm.out, prm.out_stride, prm.G, prm.Hkv, prm.ws));
   return AEG_OK;
+}
+
+// Worker warps of an attention launch on the current device (the plan cuts the work into this
+// many ranges; the attention kernel checks that its grid matches).
+int worker_warps(int G) {
+  const int per_sm = ctas_per_sm(AEG_DTYPE_FP16, G <= 8 ? 1 : 2);
+  return num_sms() * (per_sm > 0 ? per_sm : 1) * kWarps;
 }
 
 int validate_shape(int B, int Hq, int Hkv, int D, int table_stride) {
@@ -993,7 +1153,9 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   prm.G = Hq / Hkv;
   prm.Hkv = Hkv;
   prm.num_pairs = B * Hkv;
+  prm.max_warps = L.max_warps;
   prm.max_units = L.max_units;
+  prm.max_slots = L.max_slots;
   prm.num_blocks = num_blocks;
   prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
   prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
@@ -1027,14 +1189,15 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
 //
 // Limits and rules of use:
 //   * The scratch holds kNoAllocScratchBytes (32 MiB) per device. Its layout is the workspace
-//     layout with room for the units the plan actually makes (target + B*Hkv, where the target
-//     is the one aeg_decode_plan uses by default), so the need grows with B*Hkv and the GQA
-//     group: about 9.6 MB for 64 sequences x 4 KV heads x 7 query heads each. A call that
-//     would need more is rejected with AEG_ERR_INVALID_ARGUMENT before anything is enqueued.
+//     layout sized for this device's worker warps W (1184 on a 148-SM B200) instead of the
+//     largest supported count: partial rows for 2 * W units and unit records for B*Hkv + W, so
+//     the need grows with the GQA group and B*Hkv: about 8.5 MB for 64 sequences x 4 KV heads
+//     x 7 query heads each. A call that would need more is rejected with
+//     AEG_ERR_INVALID_ARGUMENT before anything is enqueued.
 //   * Nothing in the scratch has to start at zero for the first call: the plan kernel that
-//     every call enqueues writes the whole header, including the work and exit counters that
-//     the attention kernel needs at zero, and the last warp of the attention kernel sets them
-//     back to zero. (Static device memory also starts zeroed when the module is loaded.)
+//     every call enqueues writes the whole header, including the barrier counters that the
+//     attention kernel needs at zero, and the last warp of the attention kernel sets them back
+//     to zero. (Static device memory also starts zeroed when the module is loaded.)
 //   * One scratch per device means calls on one device must not overlap: two calls in flight
 //     at once on different streams race on the plan, the counters and the partials. Issue
 //     them on one stream, or order the streams.
@@ -1071,25 +1234,6 @@ int noalloc_scratch(void** ptr) {
   return AEG_OK;
 }
 
-// The workspace layout with room for max_units units (the regular layout reserves
-// kMaxTargetUnits + B*Hkv, far more than the default plan makes).
-WsLayout noalloc_layout(int B, int Hq, int Hkv, int D, int max_units) {
-  WsLayout w{};
-  const int G = Hq / Hkv;
-  const int64_t P = int64_t(B) * Hkv;
-  w.max_units = max_units;
-  size_t off = 256;
-  w.split_pairs = off;
-  off = align256(off + sizeof(int4) * P);
-  w.units = off;
-  off = align256(off + 2 * sizeof(int4) * size_t(max_units));
-  w.part_ml = off;
-  off = align256(off + sizeof(float2) * size_t(max_units) * G);
-  w.part_o = off;
-  off = align256(off + sizeof(float) * size_t(max_units) * G * D);
-  w.total = off;
-  return w;
-}
 
 }  // namespace
 
@@ -1120,20 +1264,12 @@ int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* bloc
   AEG_CHECK_ARG(workspace_bytes >= L.total, "decode_plan: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
   AEG_CHECK_ARG(B == 0 || (seq_lens != nullptr && block_tables != nullptr), "decode_plan: seq_lens/block_tables is NULL");
   AEG_CHECK_ARG(aeg::aligned(seq_lens, 4) && aeg::aligned(block_tables, 4), "decode_plan: int32 arrays must be aligned");
-  // Balanced unit count: a few units per worker warp so that the dynamic scheduler can even
-  // out the tail. AEG_DECODE_UNITS_PER_WARP overrides the factor (tuning experiments).
-  int per_warp = 2;
-  if (const char* e = std::getenv("AEG_DECODE_UNITS_PER_WARP")) {
-    const int k = std::atoi(e);
-    if (k > 0) per_warp = k;
-  }
-  const int per_sm = aeg::ctas_per_sm(AEG_DTYPE_FP16, (Hq / Hkv) <= 8 ? 1 : 2);
-  long long target = static_cast<long long>(aeg::num_sms()) * (per_sm > 0 ? per_sm : 1) * aeg::kWarps * per_warp;
-  if (target > aeg::kMaxTargetUnits) target = aeg::kMaxTargetUnits;
+  const int W = aeg::worker_warps(Hq / Hkv);
+  if (W > L.max_warps)
+    return aeg::set_error(AEG_ERR_UNSUPPORTED, "decode_plan: %d worker warps exceed the workspace's %d", W, L.max_warps);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   aeg::WsPtrs w = aeg::ws_ptrs(workspace, L);
-  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, table_stride,
-                                                          static_cast<int>(target), w);
+  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W, w);
   AEG_CHECK_LAUNCH("decode_plan");
   return AEG_OK;
 }
@@ -1169,11 +1305,8 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
   AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode_noalloc: dtype %d is not fp16/bf16", dtype);
   AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode_noalloc: null pointer");
   AEG_CHECK_ARG(aeg::aligned(seq_lens, 4) && aeg::aligned(block_tables, 4), "decode_noalloc: int32 arrays must be aligned");
-  const int per_sm = aeg::ctas_per_sm(AEG_DTYPE_FP16, (Hq / Hkv) <= 8 ? 1 : 2);
-  long long target = static_cast<long long>(aeg::num_sms()) * (per_sm > 0 ? per_sm : 1) * aeg::kWarps * 2;
-  if (target > aeg::kMaxTargetUnits) target = aeg::kMaxTargetUnits;
-  const aeg::WsLayout L =
-      aeg::noalloc_layout(B, Hq, Hkv, D, static_cast<int>(target + static_cast<long long>(B) * Hkv));
+  const int W = aeg::worker_warps(Hq / Hkv);
+  const aeg::WsLayout L = aeg::layout_for(B, Hq, Hkv, D, W);
   AEG_CHECK_ARG(L.total <= aeg::kNoAllocScratchBytes,
                 "decode_noalloc: B=%d, Hq=%d, Hkv=%d needs %zu bytes of scratch, more than the %zu bytes of the "
                 "static scratch; use aeg_paged_attn_decode with a caller-owned workspace",
@@ -1182,8 +1315,8 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
   st = aeg::noalloc_scratch(&scratch);
   if (st != AEG_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, table_stride,
-                                                          static_cast<int>(target), aeg::ws_ptrs(scratch, L));
+  aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W,
+                                                          aeg::ws_ptrs(scratch, L));
   AEG_CHECK_LAUNCH("decode_plan (noalloc)");
   return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
                             const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,

@@ -55,9 +55,9 @@ class DecodeStep:
 
     @property
     def launches_per_step(self) -> int:
-        """Kernels one step launches: the plan, then per layer the attention and its split merge
-        (fused) or the cache write, the attention and the merge (unfused)."""
-        return 1 + (2 if self.fused else 3) * self.shape.num_layers
+        """Kernels one step launches: the plan, then per layer the fused cache-write/attention
+        launch (fused) or the cache write and the attention (unfused)."""
+        return 1 + (1 if self.fused else 2) * self.shape.num_layers
 
     def run_eager(self) -> None:
         """One step on the current stream, op by op."""

@@ -394,9 +394,9 @@ def run_decode(args, world, rank, local):
             "kv_bytes_per_step": kv_step, "accumulate": "fp32",
             "l2": f"inputs larger than L2: {kv_step / 1e9:.2f} GB of K/V read per step vs 126 MB L2 (no flush)",
             "parallelism": f"{world} GPU(s), one process each, own pool and batch, no collective",
-            "launch": ("one CUDA graph per step: plan + per layer one fused cache-write/attention launch and its "
-                       "split merge (PDL)" if step.fused else
-                       "one CUDA graph per step: plan + per layer reshape_and_cache, attention, split merge (PDL)"),
+            "launch": ("one CUDA graph per step: plan + per layer one fused cache-write/attention/split-merge "
+                       "launch (PDL)" if step.fused else
+                       "one CUDA graph per step: plan + per layer reshape_and_cache and attention (PDL)"),
         },
         "kv_read_gbs": kv_step * world / (ms_step / 1e3) / 1e9,
         "hbm_frac_step": (algo["attention"] + algo["reshape_and_cache"]) * L / (ms_step / 1e3) / 1e9 / peak,
@@ -411,7 +411,7 @@ def run_decode(args, world, rank, local):
         "gpu_launches": args.steps * step.launches_per_step,
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_attn_kernel (+ decode_combine_kernel, timed together per layer call)",
+            "kernel": "decode_attn_kernel (fused cache write + attention + split merge, one launch per layer)",
             "achieved": achieved,
             "peak": peak,
             "unit": "GB/s",

@@ -144,8 +144,8 @@ AEG_API int aeg_reshape_and_cache(const void* key, const void* value, int64_t ke
  * memory of at least aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by
  * one stream at a time. The plan cuts every (sequence, KV head) into block ranges of near-equal
  * length (longest first), which the warps of a persistent kernel take from an atomic counter;
- * ranges of a split (sequence, head) are merged by a second kernel that the attention call
- * enqueues right after itself.
+ * ranges of a split (sequence, head) are merged at the end of the same launch, after a grid-wide
+ * barrier (the kernel is launched cooperatively).
  *
  * Supported: D = 128; Hq % Hkv == 0; Hq / Hkv <= 16; fp16 or bf16; 16-byte aligned K/V
  * bases; a block stride that is a multiple of 8 elements; q/out with even token strides.
@@ -186,8 +186,10 @@ AEG_API int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64
  * all given to the KV-block pool. It computes what aeg_decode_plan + aeg_paged_attn_decode compute
  * (same arguments minus the workspace) in a fixed 32 MiB scratch area per device that lives in the
  * library's static device memory; nothing is allocated by the call.
- *   - Limit: the scratch need grows with B*Hkv and Hq/Hkv (about 9.6 MB for B=64, Hkv=4, Hq=28);
- *     a call needing more than 32 MiB fails with AEG_ERR_INVALID_ARGUMENT, nothing enqueued.
+ *   - Limit: the scratch holds partial rows for 2 x the device's worker warps (about 8.6 MB at
+ *     Hq/Hkv = 7, 20 MB at 16, on a 148-SM B200) plus 48 bytes per (sequence, KV head) pair; a
+ *     call needing more than 32 MiB (over ~500K pairs at Hq/Hkv = 7, ~280K at 16) fails with
+ *     AEG_ERR_INVALID_ARGUMENT, nothing enqueued.
  *   - Nothing has to be zeroed by the caller: every call re-plans and resets the counters it uses.
  *   - The scratch is shared by all calls on a device: calls that overlap in time (e.g. on two
  *     unordered streams) race. Keep them on one stream or order them.

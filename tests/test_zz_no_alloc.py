@@ -86,10 +86,11 @@ def test_noalloc_matches_regular_entry_on_two_calls_in_a_row(cuda_device):
 
 
 def test_noalloc_rejects_a_batch_beyond_the_scratch(cuda_device):
-    # 4096 one-token sequences with a 16-head GQA group need ~54 MB of scratch, above the
-    # 32 MiB the library holds. Every buffer is valid for this shape, and the call must fail on
-    # the host before enqueuing anything.
-    B, Hq, Hkv = 4096, 16, 1
+    # 40960 one-token sequences x 8 KV heads with a 16-head GQA group: 327,680 (sequence, head)
+    # pairs need ~36 MB of scratch (48 bytes per pair on top of ~20 MB of partial rows), above
+    # the 32 MiB the library holds. Every buffer is valid for this shape, and the call must fail
+    # on the host before enqueuing anything.
+    B, Hq, Hkv = 40960, 128, 8
     kv = torch.zeros((1, 1, 2, 16, Hkv, 128), dtype=torch.float16, device=cuda_device)
     q = torch.zeros((B, Hq, 128), dtype=torch.float16, device=cuda_device)
     tables = torch.zeros((B, 1), dtype=torch.int32, device=cuda_device)
