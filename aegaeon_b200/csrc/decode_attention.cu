@@ -59,6 +59,8 @@ constexpr int kHalves = kHeadDim / 64;  // 128-byte rows per (token, head)
 constexpr int kBlockTokens = 16;
 constexpr int kMaxWarps = 4096;         // worker warps of one launch the workspace is sized for
 constexpr int kPlanThreads = 256;
+constexpr int kPlanLongUnits = 4;       // a pair with more units has them written by the whole plan CTA
+constexpr int kPlanLongPairs = 512;     // capacity of the plan's list of such pairs
 constexpr int kPlanCachedSeqs = 4096;   // sequences whose block counts the plan keeps in smem
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -220,7 +222,12 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   __shared__ long long s_red[kPlanThreads / 32];
   __shared__ int s_warp[kPlanThreads / 32];
   __shared__ int s_nb[kPlanCachedSeqs];  // blocks per sequence (first kPlanCachedSeqs sequences)
+  __shared__ int4 s_long[kPlanLongPairs];         // {pair, first unit, cuts, first slot}
+  __shared__ long long s_long_o[kPlanLongPairs];  // first item of the pair
+  __shared__ int s_long_ofs[kPlanLongPairs + 1];  // prefix sums of the pairs' unit counts
+  __shared__ int s_nlong;
   const int tid = threadIdx.x;
+  if (tid == 0) s_nlong = 0;
   const int P = B * Hkv;
   const int cap = table_stride * kBlockTokens;
   const int per = (P + kPlanThreads - 1) / kPlanThreads;
@@ -306,46 +313,84 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   for (int w = Wp + tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(U, 0, 0, 0);  // empty ranges
   for (int w = Wm + tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(S, 0, 0, 0);      // no merge items
 
-  // Pass 3: write units, split-pair entries and the workers' first-unit records.
+  // Pass 3: write units, split-pair entries and the workers' first-unit records. Unit k of a
+  // pair spans items [xa, xb) between the pair's ends and the worker starts inside it; the
+  // workers starting at xa begin with it. Pairs with many units (long sequences) are queued and
+  // their units written by all threads below, so that no thread writes dozens of them, each
+  // behind a block-table load.
+  auto emit_unit = [&](int p, long long o0, int nb, int c, int k, int u_idx, int slot_idx) {
+    const int b = p / Hkv;
+    const long long wc = workers_le(o0, I, Wp);  // first worker starting after item o0
+    const long long xa = k == 0 ? o0 : worker_start(wc + k - 1, I, Wp);
+    const long long xb = k == c ? o0 + nb : worker_start(wc + k, I, Wp);
+    const int j0 = static_cast<int>(xa - o0), j1 = static_cast<int>(xb - o0);
+    const int n = j1 - j0;
+    const int* tb = tables + static_cast<int64_t>(b) * table_stride + j0;
+    const int n_ctx = min(max(seq_lens[b], 0), cap);
+    const int4 ra = make_int4(p, j0, j1, c > 0 ? slot_idx : -1);
+    const int4 rb = make_int4(n_ctx, tb[0], n > 1 ? tb[1] : 0, n > 2 ? tb[2] : 0);
+    ws.units[2 * u_idx] = ra;
+    ws.units[2 * u_idx + 1] = rb;
+    const long long w_hi = workers_le(xa, I, Wp);
+    for (long long w = workers_le(xa - 1, I, Wp); w < w_hi; ++w) {
+      ws.warp_rec[3 * w] = make_int4(u_idx, 0, 0, 0);
+      ws.warp_rec[3 * w + 1] = ra;
+      ws.warp_rec[3 * w + 2] = rb;
+    }
+  };
   o = o_t;
   for (int p = p0; p < p1; ++p) {
-    const int b = p / Hkv;
-    const int nb = blocks_of(b);
+    const int nb = blocks_of(p / Hkv);
     if (nb == 0) {
       mark_merge(sp, mo, G);
       mo += G;
       ws.split_pairs[sp++] = make_int4(p, 0, 0, 1);
       continue;
     }
-    const int n_ctx = min(max(seq_lens[b], 0), cap);
-    const int* tb = tables + static_cast<int64_t>(b) * table_stride;
     const int c = cuts(o, nb);
-    const long long wc = workers_le(o, I, Wp);  // first worker starting after item o
     if (c > 0) {
       const int q = merge_chunks(c + 1);
       mark_merge(sp, mo, G * q);
       mo += static_cast<long long>(G) * q;
       ws.split_pairs[sp++] = make_int4(p, slot, c + 1, q);
     }
-    for (int k = 0; k <= c; ++k) {
-      const long long xa = k == 0 ? o : worker_start(wc + k - 1, I, Wp);
-      const long long xb = k == c ? o + nb : worker_start(wc + k, I, Wp);
-      const int j0 = static_cast<int>(xa - o), j1 = static_cast<int>(xb - o);
-      const int n = j1 - j0;
-      const int4 ra = make_int4(p, j0, j1, c > 0 ? slot++ : -1);
-      const int4 rb = make_int4(n_ctx, tb[j0], n > 1 ? tb[j0 + 1] : 0, n > 2 ? tb[j0 + 2] : 0);
-      ws.units[2 * u] = ra;
-      ws.units[2 * u + 1] = rb;
-      // workers whose range starts at item xa begin with this unit
-      const long long w_hi = workers_le(xa, I, Wp);
-      for (long long w = workers_le(xa - 1, I, Wp); w < w_hi; ++w) {
-        ws.warp_rec[3 * w] = make_int4(u, 0, 0, 0);
-        ws.warp_rec[3 * w + 1] = ra;
-        ws.warp_rec[3 * w + 2] = rb;
+    int queued = -1;
+    if (c + 1 > kPlanLongUnits) {
+      queued = atomicAdd(&s_nlong, 1);
+      if (queued < kPlanLongPairs) {
+        s_long[queued] = make_int4(p, u, c, slot);
+        s_long_o[queued] = o;
       }
-      ++u;
     }
+    if (queued < 0 || queued >= kPlanLongPairs)
+      for (int k = 0; k <= c; ++k) emit_unit(p, o, nb, c, k, u + k, slot + k);
+    u += c + 1;
+    if (c > 0) slot += c + 1;
     o += nb;
+  }
+  __syncthreads();
+  const int n_long = min(s_nlong, kPlanLongPairs);
+  {
+    static_assert(kPlanLongPairs == 2 * kPlanThreads, "two queued pairs per plan thread");
+    const int i0 = 2 * tid;
+    const int v0 = i0 < n_long ? s_long[i0].z + 1 : 0, v1 = i0 + 1 < n_long ? s_long[i0 + 1].z + 1 : 0;
+    int total = 0;
+    const int e0 = block_excl_scan(v0 + v1, s_warp, total);
+    s_long_ofs[i0] = e0;
+    s_long_ofs[i0 + 1] = e0 + v0;
+    if (tid == 0) s_long_ofs[kPlanLongPairs] = total;
+  }
+  __syncthreads();
+  const int n_long_units = s_long_ofs[kPlanLongPairs];
+  for (int t = tid; t < n_long_units; t += kPlanThreads) {
+    int lo = 0, hi = n_long;  // the queued pair whose units include t
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_long_ofs[mid] <= t) lo = mid; else hi = mid;
+    }
+    const int4 L = s_long[lo];
+    const int k = t - s_long_ofs[lo];
+    emit_unit(L.x, s_long_o[lo], blocks_of(L.x / Hkv), L.z, k, L.y + k, L.w + k);
   }
 }
 
