@@ -59,6 +59,7 @@ constexpr int kHalves = kHeadDim / 64;  // 128-byte rows per (token, head)
 constexpr int kBlockTokens = 16;
 constexpr int kMaxWarps = 4096;         // worker warps of one launch the workspace is sized for
 constexpr int kPlanThreads = 256;
+constexpr int kUnitCost = 1;           // plan cost of starting a pair, in blocks (query load, epilogue)
 constexpr int kPlanLongUnits = 4;       // a pair with more units has them written by the whole plan CTA
 constexpr int kPlanLongPairs = 512;     // capacity of the plan's list of such pairs
 constexpr int kPlanCachedSeqs = 4096;   // sequences whose block counts the plan keeps in smem
@@ -144,10 +145,12 @@ inline WsPtrs ws_ptrs(void* ws, const WsLayout& L) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Plan kernel (one CTA). The I (pair, block) items of the batch, in pair order, are cut into
-// Wp = min(W, I) contiguous ranges of equal size (up to one item), one per worker warp: worker
-// w < Wp starts at item floor(w * I / Wp), workers from Wp on get nothing. Units are the pieces
-// of pairs between pair ends and worker starts.
+// Plan kernel (one CTA). The (pair, block) items of the batch, in pair order, each non-empty
+// pair preceded by kUnitCost virtual items (the cost of starting a pair), form a cost axis of
+// I positions, cut into Wp = min(W, I) contiguous ranges of equal size (up to one position),
+// one per worker warp: worker w < Wp starts at position floor(w * I / Wp), workers from Wp on
+// get nothing. Units are the pieces of pairs' blocks between pair ends and worker starts; a
+// worker starting on a pair's virtual positions begins with the pair's first block.
 
 __device__ __forceinline__ int seq_blocks(const int* seq_lens, int b, int cap, bool report) {
   int n = seq_lens[b];
@@ -223,7 +226,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   __shared__ int s_warp[kPlanThreads / 32];
   __shared__ int s_nb[kPlanCachedSeqs];  // blocks per sequence (first kPlanCachedSeqs sequences)
   __shared__ int4 s_long[kPlanLongPairs];         // {pair, first unit, cuts, first slot}
-  __shared__ long long s_long_o[kPlanLongPairs];  // first item of the pair
+  __shared__ long long s_long_o[kPlanLongPairs];  // position of the pair's first block
   __shared__ int s_long_ofs[kPlanLongPairs + 1];  // prefix sums of the pairs' unit counts
   __shared__ int s_nlong;
   const int tid = threadIdx.x;
@@ -242,7 +245,10 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
 
   // Pass 1: items of this thread's pairs -> item offset of its first pair, total I.
   long long local = 0;
-  for (int p = p0; p < p1; ++p) local += blocks_of(p / Hkv);
+  for (int p = p0; p < p1; ++p) {
+    const int nb = blocks_of(p / Hkv);
+    local += nb > 0 ? nb + kUnitCost : 0;
+  }
   long long I = 0;
   const long long o_t = block_excl_scan64(local, s_red, I);
   if (I > kMaxItems) {  // beyond any pool this plan can address: plan nothing, report it
@@ -274,14 +280,14 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       n_mi += G;
       continue;
     }
-    const int c = cuts(o, nb);
+    const int c = cuts(o + kUnitCost, nb);
     n_units += c + 1;
     if (c > 0) {
       ++n_sp;
       n_slots += c + 1;
       n_mi += static_cast<long long>(G) * merge_chunks(c + 1);
     }
-    o += nb;
+    o += nb + kUnitCost;
   }
   int U = 0, S = 0, SL = 0;
   int u = block_excl_scan(n_units, s_warp, U);
@@ -332,7 +338,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     ws.units[2 * u_idx] = ra;
     ws.units[2 * u_idx + 1] = rb;
     const long long w_hi = workers_le(xa, I, Wp);
-    for (long long w = workers_le(xa - 1, I, Wp); w < w_hi; ++w) {
+    for (long long w = workers_le((k == 0 ? o0 - kUnitCost : xa) - 1, I, Wp); w < w_hi; ++w) {
       ws.warp_rec[3 * w] = make_int4(u_idx, 0, 0, 0);
       ws.warp_rec[3 * w + 1] = ra;
       ws.warp_rec[3 * w + 2] = rb;
@@ -347,7 +353,8 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       ws.split_pairs[sp++] = make_int4(p, 0, 0, 1);
       continue;
     }
-    const int c = cuts(o, nb);
+    const long long ob = o + kUnitCost;  // position of the pair's first block
+    const int c = cuts(ob, nb);
     if (c > 0) {
       const int q = merge_chunks(c + 1);
       mark_merge(sp, mo, G * q);
@@ -359,14 +366,14 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       queued = atomicAdd(&s_nlong, 1);
       if (queued < kPlanLongPairs) {
         s_long[queued] = make_int4(p, u, c, slot);
-        s_long_o[queued] = o;
+        s_long_o[queued] = ob;
       }
     }
     if (queued < 0 || queued >= kPlanLongPairs)
-      for (int k = 0; k <= c; ++k) emit_unit(p, o, nb, c, k, u + k, slot + k);
+      for (int k = 0; k <= c; ++k) emit_unit(p, ob, nb, c, k, u + k, slot + k);
     u += c + 1;
     if (c > 0) slot += c + 1;
-    o += nb;
+    o = ob + nb;
   }
   __syncthreads();
   const int n_long = min(s_nlong, kPlanLongPairs);
