@@ -59,7 +59,7 @@ constexpr int kHalves = kHeadDim / 64;  // 128-byte rows per (token, head)
 constexpr int kBlockTokens = 16;
 constexpr int kMaxWarps = 4096;         // worker warps of one launch the workspace is sized for
 constexpr int kPlanThreads = 256;
-constexpr int kUnitCost = 1;           // plan cost of starting a pair, in blocks (query load, epilogue)
+constexpr int kUnitCost = 2;           // plan cost of starting a pair, in blocks (query load, epilogue)
 constexpr int kPlanLongUnits = 4;       // a pair with more units has them written by the whole plan CTA
 constexpr int kPlanLongPairs = 512;     // capacity of the plan's list of such pairs
 constexpr int kPlanCachedSeqs = 4096;   // sequences whose block counts the plan keeps in smem
@@ -173,11 +173,24 @@ __device__ __forceinline__ long long workers_le(long long x, long long I, int W)
   return c < W ? c : W;
 }
 
-// Dimension chunks of a pair's merge: enough that a lane loads at most kMergeBatch pieces.
-__device__ __forceinline__ int merge_chunks(int ns) {
+// Shape of a pair's merge, so that every lane loads at most kMergeBatch pieces: up to
+// kMergeBatch pieces, an item merges whole 128-dim rows of a group of hg query heads (hg
+// pieces-rows per head); more pieces are cut into q dimension chunks of one head each. Encoded
+// as q | hg << 8 in the split-pair entry.
+__host__ __device__ __forceinline__ int merge_shape(int ns, int G) {
+  if (ns <= kMergeBatch) {
+    const int hg = ns == 0 ? G : min(G, kMergeBatch / ns);
+    return 1 | (hg << 8);
+  }
   int q = 1;
   while (q < 32 && ns > q * kMergeBatch) q *= 2;
-  return q;
+  return q | (1 << 8);
+}
+
+// Merge items of a pair with merge shape `shape`.
+__host__ __device__ __forceinline__ int merge_items(int shape, int G) {
+  const int q = shape & 0xff, hg = shape >> 8;
+  return ((G + hg - 1) / hg) * q;
 }
 
 // Block-wide exclusive scans of one value per thread; also return the total.
@@ -277,7 +290,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     const int nb = blocks_of(p / Hkv);
     if (nb == 0) {
       ++n_sp;
-      n_mi += G;
+      n_mi += merge_items(merge_shape(0, G), G);
       continue;
     }
     const int c = cuts(o + kUnitCost, nb);
@@ -285,7 +298,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     if (c > 0) {
       ++n_sp;
       n_slots += c + 1;
-      n_mi += static_cast<long long>(G) * merge_chunks(c + 1);
+      n_mi += merge_items(merge_shape(c + 1, G), G);
     }
     o += nb + kUnitCost;
   }
@@ -348,18 +361,19 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   for (int p = p0; p < p1; ++p) {
     const int nb = blocks_of(p / Hkv);
     if (nb == 0) {
-      mark_merge(sp, mo, G);
-      mo += G;
-      ws.split_pairs[sp++] = make_int4(p, 0, 0, 1);
+      const int shape = merge_shape(0, G), n_it = merge_items(shape, G);
+      mark_merge(sp, mo, n_it);
+      mo += n_it;
+      ws.split_pairs[sp++] = make_int4(p, 0, 0, shape);
       continue;
     }
     const long long ob = o + kUnitCost;  // position of the pair's first block
     const int c = cuts(ob, nb);
     if (c > 0) {
-      const int q = merge_chunks(c + 1);
-      mark_merge(sp, mo, G * q);
-      mo += static_cast<long long>(G) * q;
-      ws.split_pairs[sp++] = make_int4(p, slot, c + 1, q);
+      const int shape = merge_shape(c + 1, G), n_it = merge_items(shape, G);
+      mark_merge(sp, mo, n_it);
+      mo += n_it;
+      ws.split_pairs[sp++] = make_int4(p, slot, c + 1, shape);
     }
     int queued = -1;
     if (c + 1 > kPlanLongUnits) {
@@ -472,29 +486,102 @@ __device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
   return r;
 }
 
-// Split merge of one item = (cut pair, query head n, dimension chunk `chunk` of q), one warp:
-// lane = (piece group g, float4 column c) with 32 / q columns per chunk; group g takes pieces
-// g, g + q, g + 2q, ... and folds them in with a running maximum (each piece's max, sum and row
-// chunk arrive in the same round trip), then the q groups are combined by xor shuffles. An
-// empty pair (ns = 0) gets a zero row. Partials are read through L2 (ld.global.cg): other SMs
-// wrote them.
+// Split merge, one item per call, one warp. Partials are read through L2 (ld.global.cg): other
+// SMs wrote them. Pieces are folded in with a running maximum; each piece's max, sum and row
+// (chunk) arrive in the same round trip, issued before any of them is used (ordered volatile
+// loads), and the loops stop at the lane's last piece so a short merge executes only the
+// instructions of its pieces.
+//   * q == 1: the item is head group `item` of hg heads; lane c owns float4 column c of the
+//     128-dim rows, and the group's hg x ns piece rows are taken head by head. An empty pair
+//     (ns = 0) gets zero rows.
+//   * q > 1 (more than kMergeBatch pieces): the item is (head item / q, dimension chunk
+//     item % q); lane = (piece group g, float4 column c) with 32 / q columns per chunk, group g
+//     takes pieces g, g + q, ..., and the q groups are combined by xor shuffles.
 template <typename T>
-__device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, int n, int chunk, int lane) {
+__device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, int item, int lane) {
   const int G = p.G;
-  const int q = e.w, ns = e.z;
+  const int q = e.w & 0xff, hg = e.w >> 8, ns = e.z;
+  const float4* po4 = reinterpret_cast<const float4*>(p.ws.part_o);
+  const int b = e.x / p.Hkv, h = e.x % p.Hkv;
+  T* out_pair = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(h) * G * kHeadDim;
+  auto write_row = [&](int n, int col, const float4& acc, float L) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* dst = out_pair + n * kHeadDim + col * 4;
+    if (aligned(dst, 8)) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(acc.x * inv, acc.y * inv), pack2<T>(acc.z * inv, acc.w * inv));
+    } else {
+      dst[0] = from_float<T>(acc.x * inv);
+      dst[1] = from_float<T>(acc.y * inv);
+      dst[2] = from_float<T>(acc.z * inv);
+      dst[3] = from_float<T>(acc.w * inv);
+    }
+  };
+  auto fold = [&](float& M, float& L, float4& acc, const float2& ml, const float4& v) {
+    if (ml.x != -INFINITY) {
+      const float Mn = fmaxf(M, ml.x);
+      const float r = M != -INFINITY ? ex2(M - Mn) : 0.f;
+      const float w = ex2(ml.x - Mn);
+      acc.x = acc.x * r + w * v.x;
+      acc.y = acc.y * r + w * v.y;
+      acc.z = acc.z * r + w * v.z;
+      acc.w = acc.w * r + w * v.w;
+      L = L * r + w * ml.y;
+      M = Mn;
+    }
+  };
+
+  if (q == 1) {
+    const int h_lo = item * hg, h_cnt = min(hg, G - h_lo);
+    if (ns == 0) {
+      for (int j = 0; j < h_cnt; ++j) write_row(h_lo + j, lane, make_float4(0.f, 0.f, 0.f, 0.f), 0.f);
+      return;
+    }
+    const int total = min(kMergeBatch, h_cnt * ns);
+    float2 ml[kMergeBatch];
+    float4 v[kMergeBatch];
+    {
+      int piece = 0, n = h_lo;
+#pragma unroll
+      for (int s = 0; s < kMergeBatch; ++s) {
+        if (s >= total) break;
+        const int64_t row = static_cast<int64_t>(e.y + piece) * G + n;
+        ml[s] = ld_cg_f2(&p.ws.part_ml[row]);
+        v[s] = ld_cg_f4(po4 + row * (kHeadDim / 4) + lane);
+        if (++piece == ns) {
+          piece = 0;
+          ++n;
+        }
+      }
+    }
+    int piece = 0, n = h_lo;
+    float M = -INFINITY, L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMergeBatch; ++s) {
+      if (s >= total) break;
+      fold(M, L, acc, ml[s], v[s]);
+      if (++piece == ns) {
+        write_row(n, lane, acc, L);
+        piece = 0;
+        ++n;
+        M = -INFINITY;
+        L = 0.f;
+        acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    return;
+  }
+
+  const int n = item / q, chunk = item % q;
   const int lq = __ffs(q) - 1;       // q is a power of two
   const int lc = 5 - lq;             // log2 of the float4 columns per chunk
   const int c = lane & ((1 << lc) - 1), g = lane >> lc;
   const int col = (chunk << lc) + c;  // float4 column of the 128-dim row
-  const float4* po4 = reinterpret_cast<const float4*>(p.ws.part_o);
   float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int s0 = g; s0 < ns; s0 += q * kMergeBatch) {
     float2 ml[kMergeBatch];
     float4 v[kMergeBatch];
-    // All loads of the batch are issued before any of them is used (ordered volatile loads):
-    // the batch costs one round trip. Both loops stop at the lane's last piece, so a short
-    // merge executes only the instructions of its pieces.
     const int cnt = min(kMergeBatch, (ns - s0 + q - 1) >> lq);
 #pragma unroll
     for (int i = 0; i < kMergeBatch; ++i) {
@@ -506,17 +593,7 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
 #pragma unroll
     for (int i = 0; i < kMergeBatch; ++i) {
       if (i >= cnt) break;
-      if (ml[i].x != -INFINITY) {
-        const float Mn = fmaxf(M, ml[i].x);
-        const float r = M != -INFINITY ? ex2(M - Mn) : 0.f;
-        const float w = ex2(ml[i].x - Mn);
-        acc.x = acc.x * r + w * v[i].x;
-        acc.y = acc.y * r + w * v[i].y;
-        acc.z = acc.z * r + w * v[i].z;
-        acc.w = acc.w * r + w * v[i].w;
-        L = L * r + w * ml[i].y;
-        M = Mn;
-      }
+      fold(M, L, acc, ml[i], v[i]);
     }
   }
   for (int off = 1 << lc; off < 32; off <<= 1) {
@@ -537,27 +614,15 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
     L = L * r1 + Lo * r2;
     M = Mn;
   }
-  if (g == 0) {
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int b = e.x / p.Hkv, h = e.x % p.Hkv;
-    T* dst = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
-             (static_cast<int64_t>(h) * G + n) * kHeadDim + col * 4;
-    if (aligned(dst, 8)) {
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(acc.x * inv, acc.y * inv), pack2<T>(acc.z * inv, acc.w * inv));
-    } else {
-      dst[0] = from_float<T>(acc.x * inv);
-      dst[1] = from_float<T>(acc.y * inv);
-      dst[2] = from_float<T>(acc.z * inv);
-      dst[3] = from_float<T>(acc.w * inv);
-    }
-  }
+  if (g == 0) write_row(n, col, acc, L);
 }
 
 // A split-pair entry is used only if it fits this call's shape (see unit_items).
 __device__ __forceinline__ bool entry_ok(const int4& e, const AttnParams& p) {
-  const int q = e.w;
-  const bool q_ok = q == 1 || q == 2 || q == 4 || q == 8 || q == 16 || q == 32;
-  return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.z >= 0 && e.y + e.z <= p.max_slots && q_ok;
+  const int q = e.w & 0xff, hg = e.w >> 8;
+  const bool shape_ok = (q == 1 && hg >= 1 && hg <= p.G && (e.z == 0 || hg * e.z <= kMergeBatch)) ||
+                        (hg == 1 && (q == 2 || q == 4 || q == 8 || q == 16 || q == 32));
+  return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.z >= 0 && e.y + e.z <= p.max_slots && shape_ok;
 }
 
 // Waits until *ctr >= target (the grid's arrival count), for at most kWaitLimitNs.
@@ -999,7 +1064,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // The first split-pair entry of this warp's merge share (plan data, read before the barrier).
   int entry = mr.x, k = mr.y;
   const bool share_ok = mr.z >= 0 && entry >= 0 && entry <= n_entries;
-  int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1);
+  int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1 | (1 << 8));
 
   // Grid-wide barrier, then the split merge. Every thread publishes its partials (fence); the
   // CTA's warps meet at a CTA barrier and one thread per CTA arrives at the grid counter and
@@ -1021,16 +1086,16 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __syncthreads();
   if (s_go && share_ok) {
     for (int left = mr.z; left > 0; --left) {
-      if (k >= G * me.w) {  // next split-pair entry
+      if (k >= merge_items(me.w, G)) {  // next split-pair entry
         ++entry;
         k = 0;
-        me = entry < n_entries ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1);
+        me = entry < n_entries ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1 | (1 << 8));
       }
       if (!entry_ok(me, p) || k < 0) {
         if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
         break;
       }
-      merge_item<T>(p, me, k / me.w, k % me.w, lane);
+      merge_item<T>(p, me, k, lane);
       ++k;
     }
   } else if (!share_ok && lane == 0) {
