@@ -49,6 +49,8 @@ def _args():
                    help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
     p.add_argument("--compact-pool", action="store_true",
                    help="size the block pool to the blocks the batch uses (same kernels; small-case profiling)")
+    p.add_argument("--scale", type=float, default=1.0,
+                   help="cfg5 only: scale the pool, swap and copy sizes (small cases for profiling)")
     p.add_argument("--profile-run", action="store_true",
                    help="timed graph replays only: no clock pre-roll, per-launch timing, end-to-end or CPU leg")
     return p.parse_args()
@@ -440,7 +442,12 @@ def run_swap(args, world, rank, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    c = synth.SWAP_CFG
+    c = dict(synth.SWAP_CFG)
+    if args.scale != 1.0:
+        for k in ("device_blocks", "swap_blocks", "copy_pairs"):
+            c[k] = max(2, int(c[k] * args.scale))
+        c["copy_pairs"] = min(c["copy_pairs"], c["device_blocks"] // 2)
+        c["swap_blocks"] = min(c["swap_blocks"], c["device_blocks"])
     shape = (c["device_blocks"],) + layout.kv_block_shape(c["num_layers"], c["num_kv_heads"], c["head_dim"])
     kv = torch.empty(shape, dtype=c["dtype"], device=device)
     synth.random_bits_(kv, c["seed"])
@@ -490,8 +497,9 @@ def run_swap(args, world, rank, local):
         "metric": "KV-block swap GB/s", "value": best_swap, "unit": "GB/s", "n_gpus": 1, "steps": reps,
         "warmup": 2, "ms_per_step": min(res["swap_out_dma_ms"], res["swap_out_sm_ms"]), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u16", "data": "synthetic random 16-bit patterns",
-        "config": {"workload": "cfg5: 4096 scattered 917,504-byte blocks HBM -> pinned host (swap-out); "
-                               "back into fresh ids; copy_blocks 8192 pairs"},
+        "config": {"workload": f"cfg5: {n} scattered {bb:,}-byte blocks HBM -> pinned host (swap-out); "
+                               f"back into fresh ids; copy_blocks {c['copy_pairs']} pairs"
+                               + ("" if args.scale == 1.0 else f" (scaled x{args.scale})")},
         "detail_ms": res, "detail_gbs": gbs,
         "swap_frac_of_link": {"out": best_swap / res["link_d2h_gbs"],
                               "in": max(gbs["swap_in_dma_gbs"], gbs["swap_in_sm_gbs"]) / res["link_h2d_gbs"]},
