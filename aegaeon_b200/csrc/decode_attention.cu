@@ -74,7 +74,9 @@ constexpr int kStageBytes = 2 * kBoxBytes;
 // Header words of the workspace.
 constexpr int kHdrItems = 0, kHdrWarps = 1, kHdrUnits = 2, kHdrSplitPairs = 3, kHdrSlots = 4,
               kHdrMergeItems = 5, kHdrBar = 8, kHdrDone = 9;
-constexpr int kMergeBatch = 16;  // pieces a lane loads per round trip in the split merge
+constexpr int kMergeBatch = 16;      // pieces a lane loads per round trip in the split merge
+constexpr int kMergeLaneGroups = 4;  // lane groups of a small merge item (heads or piece groups)
+constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item folds per round trip
 
 // ---------------------------------------------------------------------------------------
 // Workspace layout (all offsets 256-byte aligned):
@@ -173,15 +175,13 @@ __device__ __forceinline__ long long workers_le(long long x, long long I, int W)
   return c < W ? c : W;
 }
 
-// Shape of a pair's merge, so that every lane loads at most kMergeBatch pieces: up to
-// kMergeBatch pieces, an item merges whole 128-dim rows of a group of hg query heads (hg
-// pieces-rows per head); more pieces are cut into q dimension chunks of one head each. Encoded
-// as q | hg << 8 in the split-pair entry.
+// Shape of a pair's merge (merge_small / merge_item): up to 4 pieces, an item covers the whole
+// rows of 4 query heads (hg = 4); 5..kMergeBatch pieces, one query head (hg = 1); more pieces
+// are cut into q dimension chunks of one head each, so that a lane loads at most kMergeBatch
+// pieces. Encoded as q | hg << 8 in the split-pair entry.
 __host__ __device__ __forceinline__ int merge_shape(int ns, int G) {
-  if (ns <= kMergeBatch) {
-    const int hg = ns == 0 ? G : min(G, kMergeBatch / ns);
-    return 1 | (hg << 8);
-  }
+  if (ns <= kMergeLaneGroups) return 1 | (kMergeLaneGroups << 8);  // heads mode
+  if (ns <= kMergeBatch) return 1 | (1 << 8);                        // pieces mode
   int q = 1;
   while (q < 32 && ns > q * kMergeBatch) q *= 2;
   return q | (1 << 8);
@@ -480,10 +480,107 @@ __device__ __forceinline__ float2 ld_cg_f2(const float2* ptr) {
   asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(ptr));
   return r;
 }
+// Empty volatile statement that claims to rewrite a loaded pair: placed after a batch of loads,
+// it keeps the compiler from moving the folds that use the values above later loads of the
+// batch (which would serialise the round trips).
+__device__ __forceinline__ void after_loads(float2& a, float4& b) {
+  asm volatile("" : "+f"(a.x), "+f"(a.y), "+f"(b.x), "+f"(b.y), "+f"(b.z), "+f"(b.w));
+}
+
 __device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
   float4 r;
   asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
   return r;
+}
+
+// Item of a pair with at most kMergeBatch pieces (q == 1), 4 lane groups of 8 lanes; a lane
+// owns float4 columns c, c + 8, c + 16, c + 24 of a 128-dim row.
+//   * heads mode (hg == 4, up to 4 pieces): group g takes query head item * 4 + g and folds its
+//     pieces in order. An empty pair (ns = 0) gets zero rows.
+//   * pieces mode (hg == 1, 5..16 pieces): the item is query head `item`; group g folds pieces
+//     g, g + 4, g + 8, g + 12 and the 4 groups are combined by xor shuffles.
+// Either way a lane folds at most 4 pieces, whose 16 row loads share one round trip.
+
+template <typename T, typename WriteRow>
+__device__ __forceinline__ void merge_small(const AttnParams& p, const int4& e, int item, int lane, bool by_pieces,
+                                            WriteRow& write_row) {
+  constexpr int kLanes = 32 / kMergeLaneGroups;  // lanes per group
+  constexpr int kCols = kMergeLaneGroups;        // float4 columns per lane
+  const int G = p.G, ns = e.z;
+  const int grp = lane / kLanes, c = lane % kLanes;
+  const int n = by_pieces ? item : item * kMergeLaneGroups + grp;
+  const int p0 = by_pieces ? grp : 0, pstep = by_pieces ? kMergeLaneGroups : 1;
+  const int mine = n >= G ? 0 : (by_pieces ? (ns - grp + kMergeLaneGroups - 1) / kMergeLaneGroups : ns);
+  const float4* po4 = reinterpret_cast<const float4*>(p.ws.part_o);
+  float M = -INFINITY, L = 0.f;
+  float4 acc[kCols];
+#pragma unroll
+  for (int k = 0; k < kCols; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i0 = 0; i0 < mine; i0 += kMergeHeadBatch) {
+    float2 ml[kMergeHeadBatch];
+    float4 v[kMergeHeadBatch][kCols];
+    const int cnt = min(kMergeHeadBatch, mine - i0);
+#pragma unroll
+    for (int i = 0; i < kMergeHeadBatch; ++i) {
+      if (i >= cnt) break;
+      const int64_t row = static_cast<int64_t>(e.y + p0 + (i0 + i) * pstep) * G + n;
+      ml[i] = ld_cg_f2(&p.ws.part_ml[row]);
+#pragma unroll
+      for (int k = 0; k < kCols; ++k) v[i][k] = ld_cg_f4(po4 + row * (kHeadDim / 4) + c + k * kLanes);
+    }
+#pragma unroll
+    for (int i = 0; i < kMergeHeadBatch; ++i) {
+      if (i >= cnt) break;
+#pragma unroll
+      for (int k = 0; k < kCols; ++k) after_loads(ml[i], v[i][k]);
+    }
+#pragma unroll
+    for (int i = 0; i < kMergeHeadBatch; ++i) {
+      if (i >= cnt) break;
+      if (ml[i].x != -INFINITY) {
+        const float Mn = fmaxf(M, ml[i].x);
+        const float r = M != -INFINITY ? ex2(M - Mn) : 0.f;
+        const float w = ex2(ml[i].x - Mn);
+#pragma unroll
+        for (int k = 0; k < kCols; ++k) {
+          acc[k].x = acc[k].x * r + w * v[i][k].x;
+          acc[k].y = acc[k].y * r + w * v[i][k].y;
+          acc[k].z = acc[k].z * r + w * v[i][k].z;
+          acc[k].w = acc[k].w * r + w * v[i][k].w;
+        }
+        L = L * r + w * ml[i].y;
+        M = Mn;
+      }
+    }
+  }
+  if (by_pieces) {
+#pragma unroll
+    for (int off = kLanes; off < 32; off <<= 1) {
+      const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
+      const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
+      const float Mn = fmaxf(M, Mo);
+      const float r1 = M != -INFINITY ? ex2(M - Mn) : 0.f;
+      const float r2 = Mo != -INFINITY ? ex2(Mo - Mn) : 0.f;
+#pragma unroll
+      for (int k = 0; k < kCols; ++k) {
+        float4 ao;
+        ao.x = __shfl_xor_sync(0xffffffffu, acc[k].x, off);
+        ao.y = __shfl_xor_sync(0xffffffffu, acc[k].y, off);
+        ao.z = __shfl_xor_sync(0xffffffffu, acc[k].z, off);
+        ao.w = __shfl_xor_sync(0xffffffffu, acc[k].w, off);
+        acc[k].x = acc[k].x * r1 + ao.x * r2;
+        acc[k].y = acc[k].y * r1 + ao.y * r2;
+        acc[k].z = acc[k].z * r1 + ao.z * r2;
+        acc[k].w = acc[k].w * r1 + ao.w * r2;
+      }
+      L = L * r1 + Lo * r2;
+      M = Mn;
+    }
+    if (grp != 0) return;
+  }
+  if (n >= G) return;
+#pragma unroll
+  for (int k = 0; k < kCols; ++k) write_row(n, c + k * kLanes, acc[k], L);
 }
 
 // Split merge, one item per call, one warp. Partials are read through L2 (ld.global.cg): other
@@ -491,9 +588,7 @@ __device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
 // (chunk) arrive in the same round trip, issued before any of them is used (ordered volatile
 // loads), and the loops stop at the lane's last piece so a short merge executes only the
 // instructions of its pieces.
-//   * q == 1: the item is head group `item` of hg heads; lane c owns float4 column c of the
-//     128-dim rows, and the group's hg x ns piece rows are taken head by head. An empty pair
-//     (ns = 0) gets zero rows.
+//   * q == 1: merge_small.
 //   * q > 1 (more than kMergeBatch pieces): the item is (head item / q, dimension chunk
 //     item % q); lane = (piece group g, float4 column c) with 32 / q columns per chunk, group g
 //     takes pieces g, g + q, ..., and the q groups are combined by xor shuffles.
@@ -516,7 +611,7 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
       dst[3] = from_float<T>(acc.w * inv);
     }
   };
-  auto fold = [&](float& M, float& L, float4& acc, const float2& ml, const float4& v) {
+  auto fold = [](float& M, float& L, float4& acc, const float2& ml, const float4& v) {
     if (ml.x != -INFINITY) {
       const float Mn = fmaxf(M, ml.x);
       const float r = M != -INFINITY ? ex2(M - Mn) : 0.f;
@@ -531,44 +626,7 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
   };
 
   if (q == 1) {
-    const int h_lo = item * hg, h_cnt = min(hg, G - h_lo);
-    if (ns == 0) {
-      for (int j = 0; j < h_cnt; ++j) write_row(h_lo + j, lane, make_float4(0.f, 0.f, 0.f, 0.f), 0.f);
-      return;
-    }
-    const int total = min(kMergeBatch, h_cnt * ns);
-    float2 ml[kMergeBatch];
-    float4 v[kMergeBatch];
-    {
-      int piece = 0, n = h_lo;
-#pragma unroll
-      for (int s = 0; s < kMergeBatch; ++s) {
-        if (s >= total) break;
-        const int64_t row = static_cast<int64_t>(e.y + piece) * G + n;
-        ml[s] = ld_cg_f2(&p.ws.part_ml[row]);
-        v[s] = ld_cg_f4(po4 + row * (kHeadDim / 4) + lane);
-        if (++piece == ns) {
-          piece = 0;
-          ++n;
-        }
-      }
-    }
-    int piece = 0, n = h_lo;
-    float M = -INFINITY, L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int s = 0; s < kMergeBatch; ++s) {
-      if (s >= total) break;
-      fold(M, L, acc, ml[s], v[s]);
-      if (++piece == ns) {
-        write_row(n, lane, acc, L);
-        piece = 0;
-        ++n;
-        M = -INFINITY;
-        L = 0.f;
-        acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
+    merge_small<T>(p, e, item, lane, hg == 1, write_row);
     return;
   }
 
@@ -589,6 +647,11 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
       const int64_t row = static_cast<int64_t>(e.y + s0 + (i << lq)) * G + n;
       ml[i] = ld_cg_f2(&p.ws.part_ml[row]);
       v[i] = ld_cg_f4(po4 + row * (kHeadDim / 4) + col);
+    }
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      if (i >= cnt) break;
+      after_loads(ml[i], v[i]);
     }
 #pragma unroll
     for (int i = 0; i < kMergeBatch; ++i) {
@@ -620,7 +683,7 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
 // A split-pair entry is used only if it fits this call's shape (see unit_items).
 __device__ __forceinline__ bool entry_ok(const int4& e, const AttnParams& p) {
   const int q = e.w & 0xff, hg = e.w >> 8;
-  const bool shape_ok = (q == 1 && hg >= 1 && hg <= p.G && (e.z == 0 || hg * e.z <= kMergeBatch)) ||
+  const bool shape_ok = (q == 1 && hg == 4 && e.z <= 4) || (q == 1 && hg == 1 && e.z > 4 && e.z <= kMergeBatch) ||
                         (hg == 1 && (q == 2 || q == 4 || q == 8 || q == 16 || q == 32));
   return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.z >= 0 && e.y + e.z <= p.max_slots && shape_ok;
 }
