@@ -27,14 +27,18 @@
 //     bf16 value plus its bf16 rounding residue (two MMAs) so that P V keeps ~16 mantissa bits.
 //   * A whole pair's unit writes the output rows; a split unit writes an fp32 partial (O scaled
 //     by 2^-max, max, sum). When its range is done every thread publishes its partials (one
-//     fence), the CTA's warps meet, and one thread per CTA arrives at a grid-wide barrier (the
-//     grid is launched cooperatively). Then all warps merge the split pairs: a merge item is
-//     (pair, query head, dimension chunk), sized so that every lane loads at most 16 pieces in
-//     one round trip, and the plan spreads the items evenly over the warps. Measured and
-//     rejected: signalling every split (fence + counter per split, the last one merges) cost
-//     ~2.5 us per split under full HBM load; merging each pair in the CTA that computed its
-//     last piece (per-CTA flags, no grid barrier) piled the long and the short-sequence pairs
-//     onto a few CTAs; a dynamic unit queue left ~2 us gaps at every unit change.
+//     fence), the CTA's warps meet, and one thread stamps the CTA's flag (its own cache line)
+//     with the launch's epoch. Then all warps merge the split pairs: the plan spreads the merge
+//     items evenly over the warps, and an item waits only for the flags of the CTAs that
+//     computed its pair's pieces (the grid is launched cooperatively, so they are resident). A
+//     merge item covers 4 query heads of a pair with up to 4 pieces, one head of a pair with
+//     up to 16 (in 4 lane groups), or a dimension chunk of one head beyond that, so that a lane
+//     folds at most 4 (16) pieces loaded in one round trip. Measured and rejected: signalling
+//     every split (fence + counter per split, the last one merges) cost ~2.5 us per split under
+//     full HBM load; a grid-wide barrier before the merge made every item wait for the slowest
+//     CTA; merging each pair in the CTA that computed its last piece piled the long and the
+//     short-sequence pairs onto a few CTAs; a dynamic unit queue left ~2 us gaps at every unit
+//     change; polling packed flags with short sleeps slowed the flag stores themselves.
 //   * Fused form (aeg_decode_layer): the warp that reads a sequence's newest block writes the
 //     new token's K/V row of its head into the cache and patches it into the tile.
 //   * Every wait is bounded (2 s); a timeout raises AEG_DEVERR_WAIT_TIMEOUT and the warp
@@ -73,7 +77,8 @@ constexpr int kStageBytes = 2 * kBoxBytes;
 
 // Header words of the workspace.
 constexpr int kHdrItems = 0, kHdrWarps = 1, kHdrUnits = 2, kHdrSplitPairs = 3, kHdrSlots = 4,
-              kHdrMergeItems = 5, kHdrBar = 8, kHdrDone = 9;
+              kHdrMergeItems = 5, kHdrEpoch = 8, kHdrDone = 9;
+constexpr int kFlagStride = 32;  // int32 words between CTA flags: one 128-byte line each
 constexpr int kMergeBatch = 16;      // pieces a lane loads per round trip in the split merge
 constexpr int kMergeLaneGroups = 4;  // lane groups of a small merge item (heads or piece groups)
 constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item folds per round trip
@@ -84,9 +89,13 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 //   warp_rec    : int4[3 * (max_warps + 1)]  per worker warp w: {first unit, 0, 0, 0} and a copy of
 //                            its first unit's record (one load starts a warp); entry `warps`
 //                            holds the end of the unit list
-//   split_pairs : int4[P]    {pair, first partial slot, nsplit, q} of every (sequence, head) cut
-//                            across warps (nsplit >= 2), and {pair, 0, 0, 1} of every empty one;
-//                            its merge is G * q items (query head, one of q dimension chunks)
+//   split_pairs : int4[P]    {pair, first partial slot, nsplit | shape << 16, first CTA | CTAs
+//                            << 16} of every (sequence, head) cut across warps (nsplit >= 2)
+//                            and {pair, 0, shape << 16, 0} of every empty one; its merge is
+//                            merge_items(shape) items, which wait for the CTAs that computed
+//                            its pieces
+//   cta_flag    : int32[max_warps / 8 * kFlagStride] per CTA (one cache line each): epoch + 1
+//                            once its partials are published
 //   merge_rec   : int4[max_warps]  per warp: {split-pair entry, item within it, items, 0}, its
 //                            share of the merge items (balanced like the blocks)
 //   units       : int4[2 * max_units]  {pair, j0, j1, partial slot or -1},
@@ -94,7 +103,7 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 //   part_ml     : float2[max_slots * G]        (max in log2 units, sum) per query head
 //   part_o      : float [max_slots * G * D]    partial outputs, scaled by 2^-max
 struct WsLayout {
-  size_t warp_rec, split_pairs, merge_rec, units, part_ml, part_o, total;
+  size_t warp_rec, split_pairs, cta_flag, merge_rec, units, part_ml, part_o, total;
   int max_warps, max_units, max_slots;
 };
 
@@ -114,6 +123,8 @@ WsLayout layout_for(int B, int Hq, int Hkv, int D, int max_warps) {
   off = align256(off + 3 * sizeof(int4) * size_t(max_warps + 1));
   w.split_pairs = off;
   off = align256(off + sizeof(int4) * P);
+  w.cta_flag = off;
+  off = align256(off + sizeof(int) * size_t(max_warps / kWarps) * kFlagStride);
   w.merge_rec = off;
   off = align256(off + sizeof(int4) * size_t(max_warps));
   w.units = off;
@@ -132,6 +143,7 @@ struct WsPtrs {
   int* header;
   int4* warp_rec;
   int4* split_pairs;
+  int* cta_flag;
   int4* merge_rec;
   int4* units;
   float2* part_ml;
@@ -141,7 +153,8 @@ struct WsPtrs {
 inline WsPtrs ws_ptrs(void* ws, const WsLayout& L) {
   char* b = static_cast<char*>(ws);
   return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int4*>(b + L.warp_rec),
-                reinterpret_cast<int4*>(b + L.split_pairs), reinterpret_cast<int4*>(b + L.merge_rec),
+                reinterpret_cast<int4*>(b + L.split_pairs), reinterpret_cast<int*>(b + L.cta_flag),
+                reinterpret_cast<int4*>(b + L.merge_rec),
                 reinterpret_cast<int4*>(b + L.units),
                 reinterpret_cast<float2*>(b + L.part_ml), reinterpret_cast<float*>(b + L.part_o)};
 }
@@ -270,7 +283,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       ws.header[kHdrWarps] = W;
       ws.header[kHdrUnits] = 0;
       ws.header[kHdrSplitPairs] = 0;
-      ws.header[kHdrBar] = 0;
+      ws.header[kHdrEpoch] = 0;
       ws.header[kHdrDone] = 0;
     }
     for (int w = tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(0, 0, 0, 0);
@@ -326,9 +339,10 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     ws.header[kHdrSplitPairs] = S;
     ws.header[kHdrSlots] = SL;
     ws.header[kHdrMergeItems] = static_cast<int>(MI < 0x7fffffffLL ? MI : 0x7fffffffLL);
-    ws.header[kHdrBar] = 0;
+    ws.header[kHdrEpoch] = 0;
     ws.header[kHdrDone] = 0;
   }
+  for (int c = tid; c < W / kWarps; c += kPlanThreads) ws.cta_flag[c * kFlagStride] = 0;
   for (int w = Wp + tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(U, 0, 0, 0);  // empty ranges
   for (int w = Wm + tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(S, 0, 0, 0);      // no merge items
 
@@ -364,7 +378,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       const int shape = merge_shape(0, G), n_it = merge_items(shape, G);
       mark_merge(sp, mo, n_it);
       mo += n_it;
-      ws.split_pairs[sp++] = make_int4(p, 0, 0, shape);
+      ws.split_pairs[sp++] = make_int4(p, 0, shape << 16, 0);
       continue;
     }
     const long long ob = o + kUnitCost;  // position of the pair's first block
@@ -373,7 +387,9 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       const int shape = merge_shape(c + 1, G), n_it = merge_items(shape, G);
       mark_merge(sp, mo, n_it);
       mo += n_it;
-      ws.split_pairs[sp++] = make_int4(p, slot, c + 1, shape);
+      const int cta0 = static_cast<int>((workers_le(ob, I, Wp) - 1) / kWarps);
+      const int cta1 = static_cast<int>((workers_le(ob + nb - 1, I, Wp) - 1) / kWarps);
+      ws.split_pairs[sp++] = make_int4(p, slot, (c + 1) | (shape << 16), cta0 | ((cta1 - cta0 + 1) << 16));
     }
     int queued = -1;
     if (c + 1 > kPlanLongUnits) {
@@ -506,7 +522,7 @@ __device__ __forceinline__ void merge_small(const AttnParams& p, const int4& e, 
                                             WriteRow& write_row) {
   constexpr int kLanes = 32 / kMergeLaneGroups;  // lanes per group
   constexpr int kCols = kMergeLaneGroups;        // float4 columns per lane
-  const int G = p.G, ns = e.z;
+  const int G = p.G, ns = e.z & 0xffff;
   const int grp = lane / kLanes, c = lane % kLanes;
   const int n = by_pieces ? item : item * kMergeLaneGroups + grp;
   const int p0 = by_pieces ? grp : 0, pstep = by_pieces ? kMergeLaneGroups : 1;
@@ -595,7 +611,7 @@ __device__ __forceinline__ void merge_small(const AttnParams& p, const int4& e, 
 template <typename T>
 __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, int item, int lane) {
   const int G = p.G;
-  const int q = e.w & 0xff, hg = e.w >> 8, ns = e.z;
+  const int shape = e.z >> 16, q = shape & 0xff, hg = shape >> 8, ns = e.z & 0xffff;
   const float4* po4 = reinterpret_cast<const float4*>(p.ws.part_o);
   const int b = e.x / p.Hkv, h = e.x % p.Hkv;
   T* out_pair = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(h) * G * kHeadDim;
@@ -682,18 +698,24 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
 
 // A split-pair entry is used only if it fits this call's shape (see unit_items).
 __device__ __forceinline__ bool entry_ok(const int4& e, const AttnParams& p) {
-  const int q = e.w & 0xff, hg = e.w >> 8;
-  const bool shape_ok = (q == 1 && hg == 4 && e.z <= 4) || (q == 1 && hg == 1 && e.z > 4 && e.z <= kMergeBatch) ||
+  const int shape = e.z >> 16, q = shape & 0xff, hg = shape >> 8, ns = e.z & 0xffff;
+  const int cta0 = e.w & 0xffff, n_ctas = e.w >> 16;
+  const bool shape_ok = (q == 1 && hg == 4 && ns <= 4) || (q == 1 && hg == 1 && ns > 4 && ns <= kMergeBatch) ||
                         (hg == 1 && (q == 2 || q == 4 || q == 8 || q == 16 || q == 32));
-  return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.z >= 0 && e.y + e.z <= p.max_slots && shape_ok;
+  return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.y + ns <= p.max_slots && shape_ok &&
+         cta0 + n_ctas <= static_cast<int>(gridDim.x) && (ns == 0) == (n_ctas == 0);
 }
 
-// Waits until *ctr >= target (the grid's arrival count), for at most kWaitLimitNs.
-__device__ __forceinline__ bool grid_wait(const int* ctr, int target) {
-  if (ld_acquire_gpu(ctr) >= target) return true;
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag == v (a CTA's publication stamp), for at most kWaitLimitNs.
+__device__ __forceinline__ bool flag_wait(const int* flag, int v) {
+  if (ld_acquire_gpu(flag) == v) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (ld_acquire_gpu(ctr) < target) {
-    __nanosleep(64);
+  while (ld_acquire_gpu(flag) != v) {
+    __nanosleep(256);
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
   return true;
@@ -779,12 +801,15 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     r0.x = p.ws.header[kHdrSplitPairs];
   else if (lane == 7)
     r0 = p.ws.merge_rec[gw];
+  else if (lane == 8)
+    r0.x = p.ws.header[kHdrEpoch];
   const int u_beg = __shfl_sync(0xffffffffu, r0.x, 0);
   const int u_end = __shfl_sync(0xffffffffu, r0.x, 3);
   const int planned_warps = __shfl_sync(0xffffffffu, r0.x, 4);
   const int planned_units = __shfl_sync(0xffffffffu, r0.x, 5);
   const int n_entries = min(max(__shfl_sync(0xffffffffu, r0.x, 6), 0), p.num_pairs);
   const int4 mr = shfl4(r0, 7);  // this warp's share of the split merge
+  const int epoch = __shfl_sync(0xffffffffu, r0.x, 8);
   int n_units = u_end - u_beg;
   if (!(planned_warps == total_warps && planned_units <= p.max_units && u_beg >= 0 && u_beg <= u_end &&
         u_end <= planned_units)) {
@@ -1124,53 +1149,63 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
   }
 
-  // The first split-pair entry of this warp's merge share (plan data, read before the barrier).
+  // The first split-pair entry of this warp's merge share (plan data, read early).
   int entry = mr.x, k = mr.y;
   const bool share_ok = mr.z >= 0 && entry >= 0 && entry <= n_entries;
-  int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1 | (1 << 8));
+  const int4 none = make_int4(-1, 0, (1 | (1 << 8)) << 16, 0);
+  int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : none;
 
-  // Grid-wide barrier, then the split merge. Every thread publishes its partials (fence); the
-  // CTA's warps meet at a CTA barrier and one thread per CTA arrives at the grid counter and
-  // waits for all CTAs. The grid is launched cooperatively (all CTAs resident), and the wait is
-  // bounded all the same.
-  __shared__ int s_go;
+  // Publish this CTA's partials: every thread's stores are made visible GPU-wide (fence), the
+  // CTA's warps meet, and one thread stamps the CTA's flag with this launch's epoch.
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ctas = static_cast<int>(gridDim.x);
-    int go = 1;
-    const int arrived = atomicAdd(&p.ws.header[kHdrBar], 1) + 1;
-    if (arrived < ctas && !grid_wait(&p.ws.header[kHdrBar], ctas)) {
-      go = 0;
-      atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
-    }
-    s_go = go;
-  }
-  __syncthreads();
-  if (s_go && share_ok) {
+  const int cta = static_cast<int>(blockIdx.x);
+  if (threadIdx.x == 0) st_release_gpu(&p.ws.cta_flag[cta * kFlagStride], epoch + 1);
+
+  // The split merge: the plan spreads the merge items evenly over all warps; an item waits
+  // only for the flags of the CTAs that computed its pair's pieces (lanes watch up to 32 of
+  // them at once). CTAs publish before they merge and the grid is launched cooperatively (all
+  // CTAs resident), so the waits end; they are bounded all the same.
+  int ready_entry = -1;  // entry whose producer CTAs are known to have published
+  if (share_ok) {
     for (int left = mr.z; left > 0; --left) {
-      if (k >= merge_items(me.w, G)) {  // next split-pair entry
+      if (k >= merge_items(me.z >> 16, G)) {  // next split-pair entry
         ++entry;
         k = 0;
-        me = entry < n_entries ? p.ws.split_pairs[entry] : make_int4(-1, 0, 0, 1 | (1 << 8));
+        me = entry < n_entries ? p.ws.split_pairs[entry] : none;
       }
       if (!entry_ok(me, p) || k < 0) {
         if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
         break;
       }
+      if (ready_entry != entry) {
+        const int c0 = me.w & 0xffff, nc = me.w >> 16;
+        int ok = 1;
+        for (int i = 0; i < nc && ok; i += 32) {
+          const int cc = c0 + i + lane;
+          ok = __all_sync(0xffffffffu,
+                          i + lane >= nc || cc == cta || flag_wait(&p.ws.cta_flag[cc * kFlagStride], epoch + 1));
+        }
+        __syncwarp();  // orders the lanes' acquiring flag reads before every lane's partial loads
+        if (!ok) {
+          if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+        ready_entry = entry;
+      }
       merge_item<T>(p, me, k, lane);
       ++k;
     }
-  } else if (!share_ok && lane == 0) {
+  } else if (lane == 0) {
     atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
   }
-  // The last CTA to finish resets the barrier for the next launch with this plan.
+  // The last CTA to finish moves the epoch on for the next launch with this plan.
   __syncthreads();
   if (threadIdx.x == 0) {
     const int done = atomicAdd(&p.ws.header[kHdrDone], 1);
     if (done == static_cast<int>(gridDim.x) - 1) {
-      p.ws.header[kHdrBar] = 0;
       p.ws.header[kHdrDone] = 0;
+      p.ws.header[kHdrEpoch] = epoch + 1;
     }
   }
 }
