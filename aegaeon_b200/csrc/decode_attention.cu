@@ -51,6 +51,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <mutex>
+#include <unordered_set>
 #include <type_traits>
 
 namespace aeg {
@@ -451,6 +452,7 @@ struct AttnParams {
   int64_t num_blocks;
   float scale_log2;
   int q_bulk;  // query rows are 16-byte aligned: stage them with bulk copies
+  int plan_ready;  // the plan was complete before the preceding kernel started: read it early
   // Fused cache write (decode_layer): the new token of sequence b (position seq_len - 1) is
   // written into the cache and patched into the tile that holds it.
   int fuse_write;
@@ -762,13 +764,35 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   }
   __syncwarp();
 
+  // This worker's unit range and its first unit record, in one round trip. The plan is read
+  // before waiting for the preceding kernel when the host knows that kernel did not write it
+  // (the plan was followed by an earlier attention launch on this workspace).
+  const int gw = static_cast<int>(blockIdx.x) * kWarps + warp;
+  int4 r0 = make_int4(0, 0, 0, 0);
+  auto load_plan = [&]() {
+    if (lane < 3)
+      r0 = p.ws.warp_rec[3 * gw + lane];
+    else if (lane == 3)
+      r0.x = p.ws.warp_rec[3 * (gw + 1)].x;
+    else if (lane == 4)
+      r0.x = p.ws.header[kHdrWarps];
+    else if (lane == 5)
+      r0.x = p.ws.header[kHdrUnits];
+    else if (lane == 6)
+      r0.x = p.ws.header[kHdrSplitPairs];
+    else if (lane == 7)
+      r0 = p.ws.merge_rec[gw];
+  };
+  if (p.plan_ready) load_plan();
+
   // Everything below reads data produced by earlier work on the stream.
   pdl_wait_primary();
   pdl_launch_dependents();
+  if (!p.plan_ready) load_plan();
+  const int epoch_word = lane == 0 ? p.ws.header[kHdrEpoch] : 0;  // written by the previous launch
 
   const int G = p.G;
   const int Hkv = p.Hkv;
-  const int gw = static_cast<int>(blockIdx.x) * kWarps + warp;
   const int total_warps = static_cast<int>(gridDim.x) * kWarps;
   const uint64_t pol = l2_policy_evict_first();
   const T* q = static_cast<const T*>(p.q);
@@ -787,29 +811,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     if (lane == 0) atomicOr(&g_deverr_attn, AEG_DEVERR_WAIT_TIMEOUT);
   };
 
-  // This worker's unit range and its first unit record, in one round trip.
-  int4 r0 = make_int4(0, 0, 0, 0);
-  if (lane < 3)
-    r0 = p.ws.warp_rec[3 * gw + lane];
-  else if (lane == 3)
-    r0.x = p.ws.warp_rec[3 * (gw + 1)].x;
-  else if (lane == 4)
-    r0.x = p.ws.header[kHdrWarps];
-  else if (lane == 5)
-    r0.x = p.ws.header[kHdrUnits];
-  else if (lane == 6)
-    r0.x = p.ws.header[kHdrSplitPairs];
-  else if (lane == 7)
-    r0 = p.ws.merge_rec[gw];
-  else if (lane == 8)
-    r0.x = p.ws.header[kHdrEpoch];
   const int u_beg = __shfl_sync(0xffffffffu, r0.x, 0);
   const int u_end = __shfl_sync(0xffffffffu, r0.x, 3);
   const int planned_warps = __shfl_sync(0xffffffffu, r0.x, 4);
   const int planned_units = __shfl_sync(0xffffffffu, r0.x, 5);
   const int n_entries = min(max(__shfl_sync(0xffffffffu, r0.x, 6), 0), p.num_pairs);
   const int4 mr = shfl4(r0, 7);  // this warp's share of the split merge
-  const int epoch = __shfl_sync(0xffffffffu, r0.x, 8);
   int n_units = u_end - u_beg;
   if (!(planned_warps == total_warps && planned_units <= p.max_units && u_beg >= 0 && u_beg <= u_end &&
         u_end <= planned_units)) {
@@ -1155,6 +1162,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   const int4 none = make_int4(-1, 0, (1 | (1 << 8)) << 16, 0);
   int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : none;
 
+  const int epoch = __shfl_sync(0xffffffffu, epoch_word, 0);
+
   // Publish this CTA's partials: every thread's stores are made visible GPU-wide (fence), the
   // CTA's warps meet, and one thread stamps the CTA's flag with this launch's epoch.
   __threadfence();
@@ -1322,6 +1331,22 @@ int validate_shape(int B, int Hq, int Hkv, int D, int table_stride) {
   return AEG_OK;
 }
 
+// Workspaces whose plan was launched and not yet followed by an attention launch: the first
+// attention launch after a plan may directly follow the plan kernel, so it reads the plan only
+// after waiting for the preceding kernel; later launches read it before.
+std::mutex g_fresh_mu;
+std::unordered_set<const void*> g_fresh_plans;
+
+void mark_plan_fresh(const void* ws) {
+  std::lock_guard<std::mutex> lock(g_fresh_mu);
+  g_fresh_plans.insert(ws);
+}
+
+bool take_plan_fresh(const void* ws) {
+  std::lock_guard<std::mutex> lock(g_fresh_mu);
+  return g_fresh_plans.erase(ws) > 0;
+}
+
 int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_new,
                   int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
                   int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
@@ -1374,6 +1399,7 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   prm.num_blocks = num_blocks;
   prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
   prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
+  prm.plan_ready = take_plan_fresh(workspace) ? 0 : 1;
   prm.fuse_write = fuse ? 1 : 0;
   prm.k_new = k_new;
   prm.v_new = v_new;
@@ -1486,6 +1512,7 @@ int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* bloc
   aeg::WsPtrs w = aeg::ws_ptrs(workspace, L);
   aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W, w);
   AEG_CHECK_LAUNCH("decode_plan");
+  aeg::mark_plan_fresh(workspace);
   return AEG_OK;
 }
 
@@ -1533,6 +1560,7 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
   aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W,
                                                           aeg::ws_ptrs(scratch, L));
   AEG_CHECK_LAUNCH("decode_plan (noalloc)");
+  aeg::mark_plan_fresh(scratch);
   return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
                             const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
                             Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, stream, false, &L);
