@@ -135,6 +135,30 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// Global loads with an L2 eviction-priority hint (created by l2_policy_*).
+__device__ __forceinline__ int4 ld_hint(const int4* ptr, uint64_t pol) {
+  int4 r;
+  asm volatile("ld.global.L2::cache_hint.v4.s32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(ptr), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ int ld_hint(const int* ptr, uint64_t pol) {
+  int r;
+  asm volatile("ld.global.L2::cache_hint.s32 %0, [%1], %2;" : "=r"(r) : "l"(ptr), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void st_hint(int4* ptr, const int4& v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.s32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
+}
+
 // Programmatic dependent launch -----------------------------------------------------------
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -728,7 +728,7 @@ struct AttnSmem {
   static constexpr int kQSlot = 8 * NT * kHeadDim * 2;           // query rows of one unit
   static constexpr int kPerWarp = kStages * kStageBytes + kQSlot;  // multiple of 1024
   static constexpr int kOffBars = kWarps * kPerWarp;
-  static constexpr int kBarsPerWarp = kStages + 1;
+  static constexpr int kBarsPerWarp = kStages + 2;  // stages, query slot, one scratch word
   static constexpr int kTotal = kOffBars + kWarps * kBarsPerWarp * 8;
   static constexpr size_t kDynamic = size_t(kTotal) + 1024;  // + alignment slack
   static_assert(kPerWarp % 1024 == 0, "per-warp regions must keep 1024-byte alignment");
@@ -752,6 +752,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   T* qslot = reinterpret_cast<T*>(ring + kStages * kStageBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL::kOffBars) + warp * SL::kBarsPerWarp;
   uint64_t* qbar = full + kStages;
+  uint32_t* qdep_slot = reinterpret_cast<uint32_t*>(full + kStages + 1);  // see the query-slot reuse below
 
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -768,20 +769,23 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // before waiting for the preceding kernel when the host knows that kernel did not write it
   // (the plan was followed by an earlier attention launch on this workspace).
   const int gw = static_cast<int>(blockIdx.x) * kWarps + warp;
+  // Plan data is read once per layer launch: it is kept in L2 with an evict-last hint (the K/V
+  // stream is loaded evict-first).
+  const uint64_t keep = l2_policy_evict_last();
   int4 r0 = make_int4(0, 0, 0, 0);
   auto load_plan = [&]() {
     if (lane < 3)
-      r0 = p.ws.warp_rec[3 * gw + lane];
+      r0 = ld_hint(&p.ws.warp_rec[3 * gw + lane], keep);
     else if (lane == 3)
-      r0.x = p.ws.warp_rec[3 * (gw + 1)].x;
+      r0.x = ld_hint(&p.ws.warp_rec[3 * (gw + 1)].x, keep);
     else if (lane == 4)
-      r0.x = p.ws.header[kHdrWarps];
+      r0.x = ld_hint(&p.ws.header[kHdrWarps], keep);
     else if (lane == 5)
-      r0.x = p.ws.header[kHdrUnits];
+      r0.x = ld_hint(&p.ws.header[kHdrUnits], keep);
     else if (lane == 6)
-      r0.x = p.ws.header[kHdrSplitPairs];
+      r0.x = ld_hint(&p.ws.header[kHdrSplitPairs], keep);
     else if (lane == 7)
-      r0 = p.ws.merge_rec[gw];
+      r0 = ld_hint(&p.ws.merge_rec[gw], keep);
   };
   if (p.plan_ready) load_plan();
 
@@ -831,8 +835,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   int4 ra = fa, rb = fb;
   if (lane > 0) {
     if (lane < n_units) {
-      ra = p.ws.units[2 * (u_beg + lane)];
-      rb = p.ws.units[2 * (u_beg + lane) + 1];
+      ra = ld_hint(&p.ws.units[2 * (u_beg + lane)], keep);
+      rb = ld_hint(&p.ws.units[2 * (u_beg + lane) + 1], keep);
     } else {
       ra = make_int4(0, 0, 0, -1);
       rb = make_int4(0, 0, 0, 0);
@@ -850,10 +854,11 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       bb = shfl4(rb, k & 31);
     }
   };
+  // The slot's previous rows were read into registers with plain shared loads before this is
+  // called (the caller consumes them first), so the bulk copy cannot overtake those reads.
   auto load_q = [&](int k) {
     int4 a, bb;
     rec(k, a, bb);
-    fence_proxy_async_smem();
     if (unit_items(a, bb, p) == 0) {
       if (lane == 0) mbar_arrive(qbar);
       return;
@@ -879,9 +884,13 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // the block table loaded when the walker enters the unit.
   int ik = -1, ii = 0, in_ = 0, ih = 0, ibf0 = 0, ibf1 = 0, ibf2 = 0, itbase = 0, itbl = 0;
   const int* itab = p.tables;
-  int sblk[kStages];  // block id of the tile in each stage (fused cache write)
+  int sblk[kStages];      // block id of the tile in each stage (fused cache write)
+  bool patched[kStages];  // the stage holds generic-proxy writes (fused cache write patch)
 #pragma unroll
-  for (int i = 0; i < kStages; ++i) sblk[i] = 0;
+  for (int i = 0; i < kStages; ++i) {
+    sblk[i] = 0;
+    patched[i] = false;
+  }
   auto issue_enter = [&](int k) {
     ik = k;
     ii = 0;
@@ -913,10 +922,18 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       blk = __shfl_sync(0xffffffffu, itbl, ii - itbase);
     }
     const uint32_t st = g_iss % kStages;
+    bool fence = false;
 #pragma unroll
     for (int i = 0; i < kStages; ++i)
-      if (i == static_cast<int>(st)) sblk[i] = blk;
-    fence_proxy_async_smem();  // the stage being refilled was read through the generic proxy
+      if (i == static_cast<int>(st)) {
+        sblk[i] = blk;
+        fence = patched[i];
+        patched[i] = false;
+      }
+    // A stage the warp only read needs no proxy fence before the TMA refill (the reads have
+    // completed: their results fed the MMAs); one the fused cache write patched with generic
+    // stores does.
+    if (fence) fence_proxy_async_smem();
     if (lane == 0) {
       if (static_cast<unsigned long long>(static_cast<long long>(blk)) >= static_cast<unsigned long long>(p.num_blocks))
         atomicOr(&g_deverr_attn, AEG_DEVERR_BLOCK_ID_RANGE);  // TMA zero-fills it
@@ -965,6 +982,16 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         qf[nt][ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qslot + head * kHeadDim + d) : 0u;
         qf[nt][ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qslot + head * kHeadDim + d + 8) : 0u;
       }
+    }
+    // The next unit's rows overwrite the slot: make every lane's slot reads complete first (a
+    // store of a value computed from all of them cannot issue before they have returned).
+    {
+      uint32_t dep = 0;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) dep ^= qf[nt][ks][0] ^ qf[nt][ks][1];
+      if (lane == 0) *qdep_slot = dep;
     }
     __syncwarp();
     if (c + 1 < n_units) load_q(c + 1);
@@ -1023,6 +1050,9 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
           *reinterpret_cast<uint2*>(ring + st * kStageBytes + soff) = knew;
           *reinterpret_cast<uint2*>(ring + st * kStageBytes + kBoxBytes + soff) = vnew;
           __syncwarp();
+#pragma unroll
+          for (int i = 0; i < kStages; ++i)
+            if (i == static_cast<int>(st)) patched[i] = true;
         }
 
         // S^T[16 tokens][8 heads] per n-tile.
