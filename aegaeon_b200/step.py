@@ -111,3 +111,69 @@ class DecodeStep:
 
     def output_bytes(self) -> int:
         return self.out.numel() * self.out.element_size()
+
+
+class DecodePipeline:
+    """End-to-end decode steps with the host transfers overlapped with the compute.
+
+    Two ``DecodeStep`` slots share the KV cache, each with its own input/output buffers, plan
+    workspace and CUDA graph. Step i runs in slot i % 2 on the compute stream while the inputs of
+    step i + 1 are copied into the other slot on an upload stream and the outputs of step i - 1
+    are read back on a download stream (the link is full duplex). Every step still copies its
+    own inputs from page-locked host memory and reads its own outputs back; only the order of
+    those copies relative to the kernels changes. Compute stays in step order, so a step's cache
+    writes are made before the next step's attention reads the cache, as in the reference.
+    """
+
+    def __init__(self, kv_cache: torch.Tensor, num_q_heads: int, batch: int, table_width: int, scale: float,
+                 fused: bool = True):
+        self.slots = [DecodeStep(kv_cache, num_q_heads, batch, table_width, scale, fused) for _ in range(2)]
+        dev = kv_cache.device
+        self.device = dev
+        self.up = torch.cuda.Stream(dev)
+        self.down = torch.cuda.Stream(dev)
+        self._loaded = [torch.cuda.Event() for _ in range(2)]   # slot inputs uploaded
+        self._computed = [torch.cuda.Event() for _ in range(2)]  # slot step finished (inputs free, outputs ready)
+        self._read = [torch.cuda.Event() for _ in range(2)]      # slot outputs read back (outputs free)
+
+    @property
+    def step(self) -> DecodeStep:
+        return self.slots[0]
+
+    def capture(self) -> "DecodePipeline":
+        for s in self.slots:
+            s.capture()
+        return self
+
+    def run(self, host_inputs, host_outs, steps: int) -> None:
+        """Runs ``steps`` steps; step i reads ``host_inputs[i % len]`` (dict of pinned tensors as for
+        ``DecodeStep.load_inputs``) and writes its outputs to ``host_outs[i % 2]`` (pinned). Returns
+        with all copies enqueued; the current stream waits for the last read-back."""
+        compute = torch.cuda.current_stream(self.device)
+        self.up.wait_stream(compute)
+        self.down.wait_stream(compute)
+
+        def upload(i):
+            s = i % 2
+            if i >= 2:
+                self.up.wait_event(self._computed[s])  # step i - 2 no longer reads these inputs
+            with torch.cuda.stream(self.up):
+                self.slots[s].load_inputs(**host_inputs[i % len(host_inputs)])
+                self._loaded[s].record(self.up)
+
+        upload(0)
+        for i in range(steps):
+            s = i % 2
+            if i + 1 < steps:
+                upload(i + 1)
+            compute.wait_event(self._loaded[s])
+            if i >= 2:
+                compute.wait_event(self._read[s])  # the outputs of step i - 2 have been read back
+            self.slots[s].replay()
+            self._computed[s].record(compute)
+            self.down.wait_event(self._computed[s])
+            with torch.cuda.stream(self.down):
+                host_outs[s].copy_(self.slots[s].out, non_blocking=True)
+                self._read[s].record(self.down)
+        compute.wait_stream(self.down)
+        compute.wait_stream(self.up)

@@ -257,7 +257,7 @@ def _per_launch_ms(fn_list, device, sleep_cycles=int(4e7)):
 
 def run_decode(args, world, rank, local):
     from aegaeon_b200 import ops, synth
-    from aegaeon_b200.step import DecodeStep
+    from aegaeon_b200.step import DecodePipeline, DecodeStep
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -347,19 +347,26 @@ def run_decode(args, world, rank, local):
     write_ms = _per_launch_ms(write_fns[:L], device)
     plan_ms = _per_launch_ms([lambda: step.plan.plan(step.seq_lens, step.block_tables)] * 4, device)
 
-    # End to end through the public step API with host buffers.
-    for _ in range(2):
-        step.run_from_host(host_inputs, host_out)
+    # End to end through the public step API with host buffers: every step uploads its inputs
+    # from pinned host memory and reads its outputs back, overlapped with the neighbouring
+    # steps' kernels (DecodePipeline: two buffer slots, upload and download streams).
+    pipe = DecodePipeline(kv, Hq, B, lay.width, scale, fused=not args.unfused)
+    for sl in pipe.slots:
+        sl.load_inputs(**dev_inputs)
+    pipe.capture()
+    host_outs = [host_out, torch.empty_like(host_out).pin_memory()]
+    pipe.run([host_inputs], host_outs, 4)
     torch.cuda.synchronize(device)
     _barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
-    for _ in range(args.steps):
-        step.run_from_host(host_inputs, host_out)
+    pipe.run([host_inputs], host_outs, args.steps)
     f1.record(stream)
     torch.cuda.synchronize(device)
     _barrier(world)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world, device)
+    assert torch.isfinite(host_outs[(args.steps - 1) % 2].float()).all(), "non-finite end-to-end output"
+    del pipe
 
     # Sanity: the timed outputs are finite (the work was done).
     assert torch.isfinite(step.out.float()).all(), "non-finite attention output"
@@ -408,7 +415,9 @@ def run_decode(args, world, rank, local):
             "h2d_bytes_per_step": step.input_bytes(),
             "d2h_bytes_per_step": step.output_bytes(),
             "ms_per_step": e2e_ms / args.steps,
-            "path": "aegaeon_b200.step.DecodeStep.run_from_host: pinned host inputs -> H2D, graph replay, D2H out",
+            "path": "aegaeon_b200.step.DecodePipeline.run: per step pinned host inputs -> H2D (upload stream), "
+                    "graph replay, D2H of the outputs (download stream); copies of neighbouring steps overlap "
+                    "the kernels",
         },
         "gpu_launches": args.steps * step.launches_per_step,
         "roofline": {
