@@ -25,6 +25,8 @@ AEG_DEVERR_SEQ_LEN_RANGE = 0x4
 AEG_DEVERR_WAIT_TIMEOUT = 0x8
 AEG_DEVERR_PLAN_MISMATCH = 0x10
 
+AEG_DECODE_PREFETCH = 0x1
+
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
@@ -44,10 +46,10 @@ SIGNATURES = {
     "aeg_decode_plan": (_i32, [_c_void_p, _sz, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p]),
     "aeg_paged_attn_decode": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                      _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, ctypes.c_float, _i32,
-                                     _c_void_p, _sz, _c_void_p]),
+                                     _c_void_p, _sz, _i32, _c_void_p]),
     "aeg_decode_layer": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p,
                                 _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32,
-                                ctypes.c_float, _i32, _c_void_p, _sz, _c_void_p]),
+                                ctypes.c_float, _i32, _c_void_p, _sz, _i32, _c_void_p]),
     "aeg_paged_attn_decode_noalloc": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                              _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, ctypes.c_float,
                                              _i32, _c_void_p]),

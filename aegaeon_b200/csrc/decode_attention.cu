@@ -30,7 +30,7 @@
 //     fence), the CTA's warps meet, and one thread stamps the CTA's flag (its own cache line)
 //     with the launch's epoch. Then all warps merge the split pairs: the plan spreads the merge
 //     items evenly over the warps, and an item waits only for the flags of the CTAs that
-//     computed its pair's pieces (the grid is launched cooperatively, so they are resident). A
+//     computed its pair's pieces (one CTA per SM: all CTAs are resident together). A
 //     merge item covers 4 query heads of a pair with up to 4 pieces, one head of a pair with
 //     up to 16 (in 4 lane groups), or a dimension chunk of one head beyond that, so that a lane
 //     folds at most 4 (16) pieces loaded in one round trip. Measured and rejected: signalling
@@ -452,7 +452,8 @@ struct AttnParams {
   int64_t num_blocks;
   float scale_log2;
   int q_bulk;  // query rows are 16-byte aligned: stage them with bulk copies
-  int plan_ready;  // the plan was complete before the preceding kernel started: read it early
+  int plan_ready;   // the plan was complete before the preceding kernel started: read it early
+  int prefetch_kv;  // the preceding kernel writes neither these cache blocks nor the tables
   // Fused cache write (decode_layer): the new token of sequence b (position seq_len - 1) is
   // written into the cache and patched into the tile that holds it.
   int fuse_write;
@@ -788,12 +789,15 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       r0 = ld_hint(&p.ws.merge_rec[gw], keep);
   };
   if (p.plan_ready) load_plan();
-
-  // Everything below reads data produced by earlier work on the stream.
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  if (!p.plan_ready) load_plan();
-  const int epoch_word = lane == 0 ? p.ws.header[kHdrEpoch] : 0;  // written by the previous launch
+  // With the plan complete and the cache and tables untouched by the preceding kernel, the
+  // first kStages K/V tiles are requested before waiting for that kernel (below); otherwise
+  // everything below reads data produced by earlier work on the stream.
+  const bool early = p.plan_ready && p.prefetch_kv;
+  if (!early) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    if (!p.plan_ready) load_plan();
+  }
 
   const int G = p.G;
   const int Hkv = p.Hkv;
@@ -953,6 +957,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
   };
 
+  if (early) {
+    refill();
+    pdl_wait_primary();
+    pdl_launch_dependents();
+  }
+  const int epoch_word = lane == 0 ? p.ws.header[kHdrEpoch] : 0;  // written by the previous launch
   if (n_units > 0) load_q(0);
   refill();
 
@@ -1203,8 +1213,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
   // The split merge: the plan spreads the merge items evenly over all warps; an item waits
   // only for the flags of the CTAs that computed its pair's pieces (lanes watch up to 32 of
-  // them at once). CTAs publish before they merge and the grid is launched cooperatively (all
-  // CTAs resident), so the waits end; they are bounded all the same.
+  // them at once). CTAs publish before they merge and all CTAs of the grid are resident
+  // together (one per SM), so the waits end; they are bounded all the same.
   int ready_entry = -1;  // entry whose producer CTAs are known to have published
   if (share_ok) {
     for (int left = mr.z; left > 0; --left) {
@@ -1329,17 +1339,20 @@ int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams
   if (num_sms() * per_sm * kWarps > prm.max_warps)
     return set_error(AEG_ERR_UNSUPPORTED, "decode: %d worker warps exceed the workspace's %d", num_sms() * per_sm * kWarps,
                      prm.max_warps);
-  // Cooperative: the kernel ends with a grid-wide barrier, so all of its CTAs must be resident.
-  cudaLaunchAttribute attr[2] = {pdl_attr(), {}};
-  attr[1].id = cudaLaunchAttributeCooperative;
-  attr[1].val.cooperative = 1;
+  // One CTA per SM (the occupancy limit), so all CTAs of the grid are resident together once the
+  // preceding kernels have left the SMs; the split merge's waits on other CTAs rely on that.
+  // Not a cooperative launch: a cooperative grid does not start early under programmatic
+  // dependent launch (measured: cfg2 step 0.506 -> 0.439 ms without it). The next layer's grid
+  // cannot take SMs before every CTA of this one has started (it launches only when all of them
+  // have passed griddepcontrol.launch_dependents), and every wait is bounded.
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms() * per_sm));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = AttnSmem<NT>::kDynamic;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, NT>, km, vm, prm));
   return AEG_OK;
 }
@@ -1381,7 +1394,7 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
                   int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
                   int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
                   const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
-                  size_t workspace_bytes, void* stream, bool fuse, const WsLayout* layout = nullptr) {
+                  size_t workspace_bytes, void* stream, bool fuse, int flags = 0, const WsLayout* layout = nullptr) {
   int st = validate_shape(B, Hq, Hkv, D, table_stride);
   if (st != AEG_OK) return st;
   if (B == 0) return AEG_OK;
@@ -1430,6 +1443,7 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
   prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
   prm.plan_ready = take_plan_fresh(workspace) ? 0 : 1;
+  prm.prefetch_kv = (flags & AEG_DECODE_PREFETCH) ? 1 : 0;
   prm.fuse_write = fuse ? 1 : 0;
   prm.k_new = k_new;
   prm.v_new = v_new;
@@ -1549,20 +1563,20 @@ int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32_t* bloc
 int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_cache,
                           const void* v_cache, int64_t block_stride, int64_t num_blocks, const int32_t* block_tables,
                           int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale,
-                          int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                          int dtype, void* workspace, size_t workspace_bytes, int flags, void* stream) {
   return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
                             const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
-                            Hq, Hkv, D, scale, dtype, workspace, workspace_bytes, stream, false);
+                            Hq, Hkv, D, scale, dtype, workspace, workspace_bytes, stream, false, flags);
 }
 
 int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* key_new,
                      int64_t key_stride, const void* value_new, int64_t value_stride, void* k_cache, void* v_cache,
                      int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
                      const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
-                     size_t workspace_bytes, void* stream) {
+                     size_t workspace_bytes, int flags, void* stream) {
   return aeg::decode_common(out, out_stride, q, q_stride, key_new, key_stride, value_new, value_stride, k_cache, v_cache,
                             block_stride, num_blocks, block_tables, table_stride, seq_lens, B, Hq, Hkv, D, scale, dtype,
-                            workspace, workspace_bytes, stream, true);
+                            workspace, workspace_bytes, stream, true, flags);
 }
 
 // Plan + attention + split merge in the static per-device scratch (no counterpart in the
@@ -1593,7 +1607,7 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
   aeg::mark_plan_fresh(scratch);
   return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
                             const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
-                            Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, stream, false, &L);
+                            Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, stream, false, 0, &L);
 }
 
 }  // extern "C"

@@ -21,7 +21,7 @@ import numpy as np
 import torch
 
 from . import _native
-from ._native import check, lib
+from ._native import AEG_DECODE_PREFETCH, check, lib
 from .layout import BLOCK_SIZE, block_bytes
 
 _DTYPES = {torch.float16: _native.AEG_DTYPE_FP16, torch.bfloat16: _native.AEG_DTYPE_BF16}
@@ -273,13 +273,15 @@ class DecodePlan:
 
 def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                       block_table: torch.Tensor, cache_seqlens: torch.Tensor, softmax_scale: float | None = None,
-                      out: torch.Tensor | None = None, plan: DecodePlan | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None, plan: DecodePlan | None = None,
+                      prefetch: bool = False) -> torch.Tensor:
     """Paged decode attention with one query token per sequence (vLLM FlashAttention decode call).
 
     query ``[B, Hq, D]``; key_cache/value_cache ``(N, 16, Hkv, D)`` views (any block stride);
     block_table int32 ``[B, W]``; cache_seqlens int32 ``[B]``. Returns ``out [B, Hq, D]``.
     ``plan`` must have been built for these ``cache_seqlens`` and ``W``; without one a plan is built
-    on the fly (an extra launch).
+    on the fly (an extra launch). ``prefetch=True`` promises that the kernel launched just before
+    on this stream writes neither these cache blocks nor the block table (``AEG_DECODE_PREFETCH``).
     """
     _require_cuda(query, "query")
     if query.dim() != 3 or query.stride(2) != 1 or query.stride(1) != query.size(2):
@@ -325,7 +327,8 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
                                        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0),
                                        key_cache.size(0), block_table.data_ptr(), block_table.stride(0),
                                        cache_seqlens.data_ptr(), B, Hq, Hkv, D, scale, _DTYPES[query.dtype],
-                                       plan.workspace.data_ptr(), plan.workspace.numel(), _stream(dev))
+                                       plan.workspace.data_ptr(), plan.workspace.numel(),
+                                       AEG_DECODE_PREFETCH if prefetch else 0, _stream(dev))
     check(st, "paged_attention_decode")
     return out
 
@@ -333,13 +336,13 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
 def decode_layer_flash(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
                        value_cache: torch.Tensor, block_table: torch.Tensor, cache_seqlens: torch.Tensor,
                        softmax_scale: float | None = None, out: torch.Tensor | None = None,
-                       plan: DecodePlan | None = None) -> torch.Tensor:
+                       plan: DecodePlan | None = None, prefetch: bool = False) -> torch.Tensor:
     """Cache write of each sequence's new token + decode attention, in one launch.
 
     ``key``/``value`` ``[B, Hkv, D]`` are written at position ``cache_seqlens[b] - 1`` of sequence b
     (the decode slot the reference builds, ``aegaeon/aegaeon/worker.py:628-633``), then attention runs
     over ``[0, cache_seqlens[b])``. Same result as ``reshape_and_cache_flash`` with those slots followed
-    by ``flash_attn_decode``.
+    by ``flash_attn_decode``. ``prefetch`` as for ``flash_attn_decode``.
     """
     _require_cuda(query, "query")
     if query.dim() != 3 or query.stride(2) != 1 or query.stride(1) != query.size(2):
@@ -384,22 +387,23 @@ def decode_layer_flash(query: torch.Tensor, key: torch.Tensor, value: torch.Tens
                                   key.stride(0), value.data_ptr(), value.stride(0), key_cache.data_ptr(),
                                   value_cache.data_ptr(), key_cache.stride(0), key_cache.size(0), block_table.data_ptr(),
                                   block_table.stride(0), cache_seqlens.data_ptr(), B, Hq, Hkv, D, scale,
-                                  _DTYPES[query.dtype], plan.workspace.data_ptr(), plan.workspace.numel(), _stream(dev))
+                                  _DTYPES[query.dtype], plan.workspace.data_ptr(), plan.workspace.numel(),
+                                  AEG_DECODE_PREFETCH if prefetch else 0, _stream(dev))
     check(st, "decode_layer")
     return out
 
 
 def decode_layer(out: torch.Tensor, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                  kv_cache: torch.Tensor, layer: int, block_tables: torch.Tensor, seq_lens: torch.Tensor,
-                 scale: float, plan: DecodePlan | None = None) -> None:
+                 scale: float, plan: DecodePlan | None = None, prefetch: bool = False) -> None:
     """Fused cache write + decode attention of ``layer`` over Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache."""
     kc, vc = _layer_views(kv_cache, layer)
-    decode_layer_flash(query, key, value, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan)
+    decode_layer_flash(query, key, value, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan, prefetch=prefetch)
 
 
 def paged_attention_decode(out: torch.Tensor, query: torch.Tensor, kv_cache: torch.Tensor, layer: int,
                            block_tables: torch.Tensor, seq_lens: torch.Tensor, scale: float,
-                           plan: DecodePlan | None = None) -> None:
+                           plan: DecodePlan | None = None, prefetch: bool = False) -> None:
     """Decode attention of ``layer`` over Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache, into ``out``."""
     kc, vc = _layer_views(kv_cache, layer)
-    flash_attn_decode(query, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan)
+    flash_attn_decode(query, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan, prefetch=prefetch)

@@ -64,8 +64,10 @@ class DecodeStep:
         self.plan.plan(self.seq_lens, self.block_tables)
         for layer in range(self.shape.num_layers):
             if self.fused:
+                # Each layer's launch follows the previous layer's (which writes only its own layer's
+                # rows) or the plan: its first K/V tiles may be requested before that kernel ends.
                 ops.decode_layer(self.out[layer], self.q[layer], self.k_new[layer], self.v_new[layer], self.kv_cache,
-                                 layer, self.block_tables, self.seq_lens, self.scale, plan=self.plan)
+                                 layer, self.block_tables, self.seq_lens, self.scale, plan=self.plan, prefetch=True)
             else:
                 ops.reshape_and_cache(self.k_new[layer], self.v_new[layer], self.kv_cache, layer, self.slot_mapping)
                 ops.paged_attention_decode(self.out[layer], self.q[layer], self.kv_cache, layer, self.block_tables,

@@ -144,8 +144,8 @@ AEG_API int aeg_reshape_and_cache(const void* key, const void* value, int64_t ke
  * memory of at least aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by
  * one stream at a time. The plan cuts every (sequence, KV head) into block ranges of near-equal
  * length (longest first), which the warps of a persistent kernel take from an atomic counter;
- * ranges of a split (sequence, head) are merged at the end of the same launch, after a grid-wide
- * barrier (the kernel is launched cooperatively).
+ * ranges of a split (sequence, head) are merged at the end of the same launch, each merge
+ * waiting only for the CTAs that computed its pieces.
  *
  * Supported: D = 128; Hq % Hkv == 0; Hq / Hkv <= 16; fp16 or bf16; 16-byte aligned K/V
  * bases; a block stride that is a multiple of 8 elements; q/out with even token strides.
@@ -156,11 +156,20 @@ AEG_API int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32
                             int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv, int D,
                             void* stream);
 
+/* Flags of aeg_paged_attn_decode / aeg_decode_layer. AEG_DECODE_PREFETCH: the K/V cache blocks
+ * and block tables the call reads are not written by the kernel that immediately precedes it on
+ * `stream`, so the launch may request its first K/V tiles before that kernel has finished (the
+ * query rows and new K/V rows are still read only after it). Safe between consecutive layers of
+ * one decode step (a layer writes only its own layer's rows); not after a cache write, a block
+ * copy or a swap of the same layer. */
+#define AEG_DECODE_PREFETCH 0x1
+
 AEG_API int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                           const void* k_cache, const void* v_cache, int64_t block_stride,
                           int64_t num_blocks, const int32_t* block_tables, int table_stride,
                           const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale,
-                          int dtype, void* workspace, size_t workspace_bytes, void* stream);
+                          int dtype, void* workspace, size_t workspace_bytes, int flags,
+                          void* stream);
 
 /* a6 + a7 fused. One decode layer as the reference runs it per layer (cache write of the new
  * token, then decode attention; aegaeon/aegaeon/worker.py:517-523): for every sequence b with
@@ -177,7 +186,7 @@ AEG_API int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64
                              int64_t block_stride, int64_t num_blocks, const int32_t* block_tables,
                              int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv,
                              int D, float scale, int dtype, void* workspace,
-                             size_t workspace_bytes, void* stream);
+                             size_t workspace_bytes, int flags, void* stream);
 
 /* Allocation-free decode attention. No counterpart in the reference: Aegaeon always has torch's
  * allocator at hand. This entry serves callers that cannot pass a workspace and must not have the

@@ -89,10 +89,10 @@ def test_decode_validation_on_host():
     # attention: bad dtype, misaligned cache base
     args = dict(out=p, q=p, k=p, v=p)
     st = lib.aeg_paged_attn_decode(p, 28 * 128, p, 28 * 128, p, p, 28 * 2 * 16 * 4 * 128, 64, p, 16, p, 4, 28, 4,
-                                   128, 0.1, 7, aligned, need, None)
+                                   128, 0.1, 7, aligned, need, 0, None)
     assert st == _native.AEG_ERR_INVALID_ARGUMENT and "dtype" in _native.last_error()
     st = lib.aeg_paged_attn_decode(p, 28 * 128, p, 28 * 128, p + 2, p, 28 * 2 * 16 * 4 * 128, 64, p, 16, p, 4, 28, 4,
-                                   128, 0.1, 0, aligned, need, None)
+                                   128, 0.1, 0, aligned, need, 0, None)
     assert st == _native.AEG_ERR_INVALID_ARGUMENT and "16-byte" in _native.last_error()
     del args
 

@@ -42,7 +42,7 @@ def _regular(q, kv, layer, tables, seq_lens, stream):
     st = LIB.aeg_decode_plan(ws.data_ptr(), nbytes, tables.data_ptr(), tables.stride(0), seq_lens.data_ptr(), B, Hq,
                              Hkv, D, stream)
     assert st == AEG_OK, _native.last_error()
-    st = LIB.aeg_paged_attn_decode(*_args(out, q, kv, layer, tables, seq_lens), ws.data_ptr(), nbytes, stream)
+    st = LIB.aeg_paged_attn_decode(*_args(out, q, kv, layer, tables, seq_lens), ws.data_ptr(), nbytes, 0, stream)
     assert st == AEG_OK, _native.last_error()
     return out
 
