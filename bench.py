@@ -378,7 +378,16 @@ def run_decode(args, world, rank, local):
     kv_step = algo["kv_read"] * L
     attn_avg_ms = statistics.mean(attn_ms)
     launch_bytes = algo["attention"] + (algo["reshape_and_cache"] if step.fused else 0)
-    achieved = launch_bytes / (attn_avg_ms / 1e3) / 1e9
+    # The dominant kernel's duration in the timed steps: the step time (CUDA events over the timed
+    # region) less the plan launch, per layer launch. Inside the step graph consecutive layer
+    # launches overlap through programmatic dependent launch, so this is the time a layer adds to
+    # the step; an isolated launch (events around it alone) also carries launch latency.
+    plan_med_ms = statistics.median(plan_ms)
+    in_step_ms = max((ms / args.steps - plan_med_ms) / L, 1e-6)
+    if not step.fused:
+        in_step_ms = max((ms / args.steps - plan_med_ms - L * statistics.median(write_ms)) / L, 1e-6)
+    achieved = launch_bytes / (in_step_ms / 1e3) / 1e9
+    achieved_isolated = launch_bytes / (attn_avg_ms / 1e3) / 1e9
     peak, peak_src = _peaks()
     traffic = _ncu_traffic(f"decode_attn_{cfg.name}")
 
@@ -430,7 +439,11 @@ def run_decode(args, world, rank, local):
             "peak_source": peak_src,
             "traffic": traffic,
             "algorithmic_bytes_per_launch": launch_bytes,
+            "duration": "per layer launch in the timed step graph: (step - plan) / layers",
+            "in_step_launch_us": in_step_ms * 1e3,
             "avg_launch_us": attn_avg_ms * 1e3,
+            "achieved_isolated_launch": achieved_isolated,
+            "frac_isolated_launch": achieved_isolated / peak,
             "launches_timed": len(attn_ms),
             "reshape_and_cache_median_us": statistics.median(write_ms) * 1e3,
             "plan_median_us": statistics.median(plan_ms) * 1e3,
