@@ -177,17 +177,40 @@ __device__ __forceinline__ int seq_blocks(const int* seq_lens, int b, int cap, b
   return (n + kBlockTokens - 1) / kBlockTokens;
 }
 
-// First item of worker w. Products stay below 2^63: I <= kMaxItems and w, W <= kMaxWarps.
+// Division of non-negative 64-bit values below 2^63 by a divisor fixed for the whole plan:
+// a multiply-high by m = floor((2^64 - 1) / d) and one correction step (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994). m * d >= 2^64 - d,
+// so n * m / 2^64 > n / d - 1/2 for n < 2^63 and the estimate is floor(n / d) or one less.
+struct InvariantDiv {
+  unsigned long long d, m;
+  __device__ explicit InvariantDiv(long long divisor)
+      : d(static_cast<unsigned long long>(divisor)), m(divisor > 0 ? ~0ULL / d : 0ULL) {}
+  __device__ __forceinline__ long long operator()(long long n) const {
+    const unsigned long long un = static_cast<unsigned long long>(n);
+    unsigned long long q = __umul64hi(un, m);
+    if (un - q * d >= d) ++q;
+    return static_cast<long long>(q);
+  }
+};
+
+// Products stay below 2^63: I <= kMaxItems and w, W <= kMaxWarps.
 constexpr long long kMaxItems = 1LL << 48;
 
-__device__ __forceinline__ long long worker_start(long long w, long long I, int W) { return w * I / W; }
-
-// Number of workers whose first item is <= x (worker 0 starts at item 0).
-__device__ __forceinline__ long long workers_le(long long x, long long I, int W) {
-  if (x < 0) return 0;
-  const long long c = ((x + 1) * W + I - 1) / I;
-  return c < W ? c : W;
-}
+// Cuts of a cost axis of I positions into W equal ranges: worker w starts at floor(w * I / W).
+struct EqualCuts {
+  long long I;
+  int W;
+  InvariantDiv by_w, by_i;
+  __device__ EqualCuts(long long I_, int W_) : I(I_), W(W_), by_w(W_), by_i(I_) {}
+  // First position of worker w.
+  __device__ __forceinline__ long long start(long long w) const { return by_w(w * I); }
+  // Number of workers whose first position is <= x (worker 0 starts at position 0).
+  __device__ __forceinline__ long long le(long long x) const {
+    if (x < 0) return 0;
+    const long long c = by_i((x + 1) * W + I - 1);
+    return c < W ? c : W;
+  }
+};
 
 // Shape of a pair's merge (merge_small / merge_item): up to 4 pieces, an item covers the whole
 // rows of 4 query heads (hg = 4); 5..kMergeBatch pieces, one query head (hg = 1); more pieces
@@ -292,8 +315,9 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     return;
   }
   const int Wp = I < W ? static_cast<int>(I) : W;  // workers with items; their starts are distinct
+  const EqualCuts wk(I, Wp);
   auto cuts = [&](long long o, int nb) {  // workers starting strictly inside the pair's items
-    return static_cast<int>(workers_le(o + nb - 1, I, Wp) - workers_le(o, I, Wp));
+    return static_cast<int>(wk.le(o + nb - 1) - wk.le(o));
   };
 
   // Pass 2: units, split-pair entries, partial slots and merge items of this thread's pairs.
@@ -323,13 +347,14 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   long long MI = 0;
   long long mo = block_excl_scan64(n_mi, s_red, MI);
   const int Wm = MI < W ? static_cast<int>(MI) : W;  // warps with merge items
+  const EqualCuts mk(MI, Wm);
   // Warps whose share of the merge items starts in [mo0, mo0 + n) get {entry, item within it,
   // items}; warp w's share is [floor(w * MI / Wm), floor((w + 1) * MI / Wm)).
   auto mark_merge = [&](int entry, long long mo0, int n) {
-    const long long w_hi = workers_le(mo0 + n - 1, MI, Wm);
-    for (long long w = workers_le(mo0 - 1, MI, Wm); w < w_hi; ++w) {
-      const long long st = worker_start(w, MI, Wm);
-      const long long en = w + 1 < Wm ? worker_start(w + 1, MI, Wm) : MI;
+    const long long w_hi = mk.le(mo0 + n - 1);
+    for (long long w = mk.le(mo0 - 1); w < w_hi; ++w) {
+      const long long st = mk.start(w);
+      const long long en = w + 1 < Wm ? mk.start(w + 1) : MI;
       ws.merge_rec[w] = make_int4(entry, static_cast<int>(st - mo0), static_cast<int>(en - st), 0);
     }
   };
@@ -354,9 +379,9 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
   // behind a block-table load.
   auto emit_unit = [&](int p, long long o0, int nb, int c, int k, int u_idx, int slot_idx) {
     const int b = p / Hkv;
-    const long long wc = workers_le(o0, I, Wp);  // first worker starting after item o0
-    const long long xa = k == 0 ? o0 : worker_start(wc + k - 1, I, Wp);
-    const long long xb = k == c ? o0 + nb : worker_start(wc + k, I, Wp);
+    const long long wc = wk.le(o0);  // first worker starting after item o0
+    const long long xa = k == 0 ? o0 : wk.start(wc + k - 1);
+    const long long xb = k == c ? o0 + nb : wk.start(wc + k);
     const int j0 = static_cast<int>(xa - o0), j1 = static_cast<int>(xb - o0);
     const int n = j1 - j0;
     const int* tb = tables + static_cast<int64_t>(b) * table_stride + j0;
@@ -365,8 +390,8 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     const int4 rb = make_int4(n_ctx, tb[0], n > 1 ? tb[1] : 0, n > 2 ? tb[2] : 0);
     ws.units[2 * u_idx] = ra;
     ws.units[2 * u_idx + 1] = rb;
-    const long long w_hi = workers_le(xa, I, Wp);
-    for (long long w = workers_le((k == 0 ? o0 - kUnitCost : xa) - 1, I, Wp); w < w_hi; ++w) {
+    const long long w_hi = wk.le(xa);
+    for (long long w = wk.le((k == 0 ? o0 - kUnitCost : xa) - 1); w < w_hi; ++w) {
       ws.warp_rec[3 * w] = make_int4(u_idx, 0, 0, 0);
       ws.warp_rec[3 * w + 1] = ra;
       ws.warp_rec[3 * w + 2] = rb;
@@ -388,8 +413,8 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       const int shape = merge_shape(c + 1, G), n_it = merge_items(shape, G);
       mark_merge(sp, mo, n_it);
       mo += n_it;
-      const int cta0 = static_cast<int>((workers_le(ob, I, Wp) - 1) / kWarps);
-      const int cta1 = static_cast<int>((workers_le(ob + nb - 1, I, Wp) - 1) / kWarps);
+      const int cta0 = static_cast<int>((wk.le(ob) - 1) / kWarps);
+      const int cta1 = static_cast<int>((wk.le(ob + nb - 1) - 1) / kWarps);
       ws.split_pairs[sp++] = make_int4(p, slot, (c + 1) | (shape << 16), cta0 | ((cta1 - cta0 + 1) << 16));
     }
     int queued = -1;
