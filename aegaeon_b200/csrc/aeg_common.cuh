@@ -159,6 +159,12 @@ __device__ __forceinline__ void st_hint(int4* ptr, const int4& v, uint64_t pol) 
                : "memory");
 }
 
+// Requests the 128-byte line holding `ptr` into L2. No data reaches the SM, so a later load
+// after a grid-dependency wait still sees the preceding kernel's writes (L2 is coherent).
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 // Programmatic dependent launch -----------------------------------------------------------
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

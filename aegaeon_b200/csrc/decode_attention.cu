@@ -26,9 +26,11 @@
 //     and accumulates O^T += V^T P^T (V fragments by ldmatrix.trans). For bf16, P enters as a
 //     bf16 value plus its bf16 rounding residue (two MMAs) so that P V keeps ~16 mantissa bits.
 //   * A whole pair's unit writes the output rows; a split unit writes an fp32 partial (O scaled
-//     by 2^-max, max, sum). When its range is done every thread publishes its partials (one
-//     fence), the CTA's warps meet, and one thread stamps the CTA's flag (its own cache line)
-//     with the launch's epoch. Then all warps merge the split pairs: the plan spreads the merge
+//     by 2^-max, max, sum). When its range is done the CTA's warps meet and one thread stamps
+//     the CTA's flag (its own cache line) with the launch's epoch by a release store. Every CTA
+//     stamps its flag once per launch, so all flags hold the same value between launches (the
+//     plan zeroes them) and a CTA takes the epoch from its own flag, with no end-of-launch
+//     counter. Then all warps merge the split pairs: the plan spreads the merge
 //     items evenly over the warps, and an item waits only for the flags of the CTAs that
 //     computed its pair's pieces (one CTA per SM: all CTAs are resident together). A
 //     merge item covers 4 query heads of a pair with up to 4 pieces, one head of a pair with
@@ -78,7 +80,7 @@ constexpr int kStageBytes = 2 * kBoxBytes;
 
 // Header words of the workspace.
 constexpr int kHdrItems = 0, kHdrWarps = 1, kHdrUnits = 2, kHdrSplitPairs = 3, kHdrSlots = 4,
-              kHdrMergeItems = 5, kHdrEpoch = 8, kHdrDone = 9;
+              kHdrMergeItems = 5;
 constexpr int kFlagStride = 32;  // int32 words between CTA flags: one 128-byte line each
 constexpr int kMergeBatch = 16;      // pieces a lane loads per round trip in the split merge
 constexpr int kMergeLaneGroups = 4;  // lane groups of a small merge item (heads or piece groups)
@@ -86,7 +88,7 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 
 // ---------------------------------------------------------------------------------------
 // Workspace layout (all offsets 256-byte aligned):
-//   header      : int32[64]  {items, warps, units, split pairs, partial slots, .., barrier, done}
+//   header      : int32[64]  {items, warps, units, split pairs, partial slots, merge items}
 //   warp_rec    : int4[3 * (max_warps + 1)]  per worker warp w: {first unit, 0, 0, 0} and a copy of
 //                            its first unit's record (one load starts a warp); entry `warps`
 //                            holds the end of the unit list
@@ -95,8 +97,8 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 //                            and {pair, 0, shape << 16, 0} of every empty one; its merge is
 //                            merge_items(shape) items, which wait for the CTAs that computed
 //                            its pieces
-//   cta_flag    : int32[max_warps / 8 * kFlagStride] per CTA (one cache line each): epoch + 1
-//                            once its partials are published
+//   cta_flag    : int32[max_warps / 8 * kFlagStride] per CTA (one cache line each): the
+//                            number of launches with this plan whose partials it has published
 //   merge_rec   : int4[max_warps]  per warp: {split-pair entry, item within it, items, 0}, its
 //                            share of the merge items (balanced like the blocks)
 //   units       : int4[2 * max_units]  {pair, j0, j1, partial slot or -1},
@@ -307,11 +309,10 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       ws.header[kHdrWarps] = W;
       ws.header[kHdrUnits] = 0;
       ws.header[kHdrSplitPairs] = 0;
-      ws.header[kHdrEpoch] = 0;
-      ws.header[kHdrDone] = 0;
     }
     for (int w = tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(0, 0, 0, 0);
     for (int w = tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(0, 0, 0, 0);
+    for (int c = tid; c < W / kWarps; c += kPlanThreads) ws.cta_flag[c * kFlagStride] = 0;
     return;
   }
   const int Wp = I < W ? static_cast<int>(I) : W;  // workers with items; their starts are distinct
@@ -365,8 +366,6 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     ws.header[kHdrSplitPairs] = S;
     ws.header[kHdrSlots] = SL;
     ws.header[kHdrMergeItems] = static_cast<int>(MI < 0x7fffffffLL ? MI : 0x7fffffffLL);
-    ws.header[kHdrEpoch] = 0;
-    ws.header[kHdrDone] = 0;
   }
   for (int c = tid; c < W / kWarps; c += kPlanThreads) ws.cta_flag[c * kFlagStride] = 0;
   for (int w = Wp + tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(U, 0, 0, 0);  // empty ranges
@@ -743,7 +742,7 @@ __device__ __forceinline__ bool flag_wait(const int* flag, int v) {
   if (ld_acquire_gpu(flag) == v) return true;
   const uint64_t t0 = globaltimer_ns();
   while (ld_acquire_gpu(flag) != v) {
-    __nanosleep(256);
+    __nanosleep(32);  // each poll waits for its load; the sleep only spaces the polls a little
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
   return true;
@@ -984,10 +983,24 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
   if (early) {
     refill();
+    // The first unit's query rows are requested into L2 only (no data reaches the SM before the
+    // wait), so that their load after the wait is an L2 hit.
+    // Every address lies inside the rows: the row start, then the starts of the later lines.
+    if (n_units > 0 && unit_items(fa, fb, p) > 0) {
+      const T* qrow = q + static_cast<int64_t>(fa.x / Hkv) * p.q_stride +
+                      static_cast<int64_t>(fa.x % Hkv) * G * kHeadDim;
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(qrow);
+      const uintptr_t line0 = a0 & ~static_cast<uintptr_t>(127);
+      const uintptr_t a1 = a0 + static_cast<uintptr_t>(G) * kHeadDim * sizeof(T);
+      if (lane < static_cast<int>((a1 - line0 + 127) / 128))
+        prefetch_l2(reinterpret_cast<const void*>(lane == 0 ? a0 : line0 + 128 * static_cast<uintptr_t>(lane)));
+    }
     pdl_wait_primary();
     pdl_launch_dependents();
   }
-  const int epoch_word = lane == 0 ? p.ws.header[kHdrEpoch] : 0;  // written by the previous launch
+  // Launches with this plan so far: this CTA's own flag, which every CTA of every earlier launch
+  // stamped once (written by the previous launch, read after waiting for it).
+  const int epoch_word = lane == 0 ? ld_acquire_gpu(&p.ws.cta_flag[blockIdx.x * kFlagStride]) : 0;
   if (n_units > 0) load_q(0);
   refill();
 
@@ -1223,18 +1236,20 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
   // The first split-pair entry of this warp's merge share (plan data, read early).
   int entry = mr.x, k = mr.y;
-  const bool share_ok = mr.z >= 0 && entry >= 0 && entry <= n_entries;
+  const bool share_ok = planned_warps == total_warps && mr.z >= 0 && entry >= 0 && entry <= n_entries;
   const int4 none = make_int4(-1, 0, (1 | (1 << 8)) << 16, 0);
   int4 me = (share_ok && mr.z > 0 && entry < n_entries) ? p.ws.split_pairs[entry] : none;
 
   const int epoch = __shfl_sync(0xffffffffu, epoch_word, 0);
+  const int stamp = static_cast<int>(static_cast<unsigned>(epoch) + 1u);  // this launch's flag value
 
-  // Publish this CTA's partials: every thread's stores are made visible GPU-wide (fence), the
-  // CTA's warps meet, and one thread stamps the CTA's flag with this launch's epoch.
-  __threadfence();
+  // Publish this CTA's partials: the CTA's warps meet, then one thread stamps the CTA's flag
+  // with a release store. The barrier orders every thread's partial stores before that store,
+  // and a release is cumulative, so a reader that acquires the stamp sees all of them (no fence
+  // in every thread).
   __syncthreads();
   const int cta = static_cast<int>(blockIdx.x);
-  if (threadIdx.x == 0) st_release_gpu(&p.ws.cta_flag[cta * kFlagStride], epoch + 1);
+  if (threadIdx.x == 0) st_release_gpu(&p.ws.cta_flag[cta * kFlagStride], stamp);
 
   // The split merge: the plan spreads the merge items evenly over all warps; an item waits
   // only for the flags of the CTAs that computed its pair's pieces (lanes watch up to 32 of
@@ -1258,7 +1273,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         for (int i = 0; i < nc && ok; i += 32) {
           const int cc = c0 + i + lane;
           ok = __all_sync(0xffffffffu,
-                          i + lane >= nc || cc == cta || flag_wait(&p.ws.cta_flag[cc * kFlagStride], epoch + 1));
+                          i + lane >= nc || cc == cta || flag_wait(&p.ws.cta_flag[cc * kFlagStride], stamp));
         }
         __syncwarp();  // orders the lanes' acquiring flag reads before every lane's partial loads
         if (!ok) {
@@ -1272,15 +1287,6 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
   } else if (lane == 0) {
     atomicOr(&g_deverr_attn, AEG_DEVERR_PLAN_MISMATCH);
-  }
-  // The last CTA to finish moves the epoch on for the next launch with this plan.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int done = atomicAdd(&p.ws.header[kHdrDone], 1);
-    if (done == static_cast<int>(gridDim.x) - 1) {
-      p.ws.header[kHdrDone] = 0;
-      p.ws.header[kHdrEpoch] = epoch + 1;
-    }
   }
 }
 
