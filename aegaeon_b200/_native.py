@@ -27,6 +27,8 @@ AEG_DEVERR_PLAN_MISMATCH = 0x10
 
 AEG_DECODE_PREFETCH = 0x1
 
+AEG_IPC_HANDLE_BYTES = 96
+
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
@@ -40,6 +42,11 @@ SIGNATURES = {
     "aeg_swap": (_i32, [_c_void_p, _c_void_p, _sz, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _c_void_p]),
     "aeg_swap_sm": (_i32, [_c_void_p, _c_void_p, _sz, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _c_void_p]),
     "aeg_copy_blocks": (_i32, [_c_void_p, _sz, _i64, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "aeg_ipc_export": (_i32, [_c_void_p, _c_void_p]),
+    "aeg_ipc_open": (_i32, [_c_void_p, ctypes.POINTER(_c_void_p), ctypes.POINTER(_i64)]),
+    "aeg_ipc_close": (_i32, [_c_void_p]),
+    "aeg_migrate_blocks": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "aeg_migrate_blocks_dma": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "aeg_reshape_and_cache": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                      _c_void_p, _i64, _i32, _i32, _c_void_p]),
     "aeg_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),

@@ -47,6 +47,13 @@ __host__ __device__ inline bool aligned(const void* p, uintptr_t a) { return (re
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// Whole-block copy kernel launch (block_copy.cu): dst_pool[d_dst[i]] <- src_pool[d_src[i]] for
+// i < n, DEVICE id arrays, ids out of range skipped and reported. Either pool may be a peer
+// GPU's memory or mapped host memory that the current device can address.
+int launch_block_copy(const void* src_pool, void* dst_pool, size_t block_bytes, int64_t n_src, int64_t n_dst,
+                      const int64_t* d_src, const int64_t* d_dst, int64_t n, cudaStream_t stream,
+                      const char* what);
+
 // Per-translation-unit readers of the sticky device error words; OR-ed by
 // aeg_read_device_errors.
 uint32_t deverr_read_and_clear_copy(cudaStream_t s, cudaError_t* err);

@@ -8,6 +8,8 @@
 //   * aeg_swap_sm    moves any number of scattered blocks with one kernel that streams 16-byte
 //                    vectors between HBM and the mapped host pool (no per-block submission).
 //   * aeg_copy_blocks the same kernel with both sides in HBM.
+//   * aeg_migrate_blocks (migrate.cu) the same kernel between this GPU's pool and a peer GPU's
+//                    pool over NVLink.
 // All paths are byte copies: bit-exact for any dtype and any bit pattern.
 #include "aeg_common.cuh"
 
@@ -75,6 +77,8 @@ block_copy_byte_kernel(const uint8_t* __restrict__ src_pool, uint8_t* __restrict
   }
 }
 
+}  // namespace
+
 int launch_block_copy(const void* src_pool, void* dst_pool, size_t block_bytes, int64_t n_src, int64_t n_dst,
                       const int64_t* d_src, const int64_t* d_dst, int64_t n, cudaStream_t stream,
                       const char* what) {
@@ -97,8 +101,6 @@ int launch_block_copy(const void* src_pool, void* dst_pool, size_t block_bytes, 
   AEG_CHECK_LAUNCH(what);
   return AEG_OK;
 }
-
-}  // namespace
 
 uint32_t deverr_read_and_clear_copy(cudaStream_t s, cudaError_t* err) {
   uint32_t v = 0, zero = 0;

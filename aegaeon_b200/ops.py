@@ -150,6 +150,129 @@ def copy_blocks(src_ids, dst_ids, kv_cache: torch.Tensor) -> None:
 
 
 # --------------------------------------------------------------------------------------------
+# GPU <-> GPU block migration. The reference stubs this path (Worker.register_kvcache_mem_handles
+# and Worker.migrate_blocks, aegaeon/aegaeon/worker.py:841-872; BlockManager._migrate_requests,
+# aegaeon/aegaeon/block_manager.py:876-950): the target engine opens the source engine's KV-cache
+# IPC handles (aegaeon/aegaeon/cuda_wrapper.py:190-208) and copies each request's blocks into
+# blocks of its own pool.
+
+IPC_HANDLE_BYTES = _native.AEG_IPC_HANDLE_BYTES
+
+
+def export_kv_cache(kv_cache: torch.Tensor) -> bytes:
+    """The IPC handle of a device block pool, for ``open_kv_cache`` in another process.
+
+    ``kv_cache`` must live in memory from cudaMalloc (PyTorch's default allocator). The handle is
+    plain bytes; send it through any host channel (``torch.distributed`` object collectives, a
+    store, a pipe). The exporter keeps ``kv_cache`` alive while others have it open.
+    """
+    _require_cuda(kv_cache, "kv_cache")
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    with torch.cuda.device(kv_cache.device):
+        check(lib.aeg_ipc_export(kv_cache.data_ptr(), buf), "ipc_export")
+    return buf.raw
+
+
+class PeerKVCache:
+    """Another process's block pool mapped into this process (``aeg_ipc_open``).
+
+    ``num_blocks`` and ``block_bytes`` describe the pool (the exporter's ``kv_cache.size(0)`` and
+    ``layout.block_bytes(kv_cache)``); the mapping must cover them. ``close()`` (or leaving a
+    ``with`` block) unmaps it once the work that reads it has completed.
+    """
+
+    def __init__(self, handle: bytes, num_blocks: int, block_bytes_: int):
+        if not isinstance(handle, (bytes, bytearray)) or len(handle) != IPC_HANDLE_BYTES:
+            raise ValueError(f"an IPC handle is {IPC_HANDLE_BYTES} bytes")
+        if num_blocks < 0 or block_bytes_ <= 0:
+            raise ValueError("num_blocks must be >= 0 and block_bytes positive")
+        ptr = ctypes.c_void_p()
+        avail = ctypes.c_int64()
+        check(lib.aeg_ipc_open(bytes(handle), ctypes.byref(ptr), ctypes.byref(avail)), "ipc_open")
+        self.ptr = int(ptr.value or 0)
+        self.num_blocks = int(num_blocks)
+        self.block_bytes = int(block_bytes_)
+        if num_blocks * block_bytes_ > avail.value:
+            self.close()
+            raise ValueError(f"the mapped pool holds {avail.value} bytes, fewer than "
+                             f"{num_blocks} blocks x {block_bytes_} bytes")
+
+    def close(self) -> None:
+        if self.ptr:
+            ptr, self.ptr = self.ptr, 0
+            check(lib.aeg_ipc_close(ptr), "ipc_close")
+
+    def __enter__(self) -> "PeerKVCache":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+def open_kv_cache(handle: bytes, num_blocks: int, block_bytes_: int) -> PeerKVCache:
+    """Maps a pool exported by ``export_kv_cache`` in another process."""
+    return PeerKVCache(handle, num_blocks, block_bytes_)
+
+
+def _pool(p, name: str) -> tuple[int, int, int, torch.device | None]:
+    """(address, blocks, block bytes, device of a local tensor or None) of a migration pool."""
+    if isinstance(p, PeerKVCache):
+        if not p.ptr:
+            raise ValueError(f"{name} is closed")
+        return p.ptr, p.num_blocks, p.block_bytes, None
+    _require_cuda(p, name)
+    if not p.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return p.data_ptr(), p.size(0), block_bytes(p), p.device
+
+
+def migrate_blocks(source_block_ids, target_block_ids, source, target, *, engine: str = "sm") -> None:
+    """``target[target_block_ids[i]] <- source[source_block_ids[i]]`` for whole multi-layer blocks
+    between two GPUs' pools.
+
+    ``source`` / ``target`` are device tensors of this process (on any GPU it can reach) or
+    ``PeerKVCache`` mappings of another process's pool. The work runs on the device of ``target``
+    when it is a tensor (a pull, as the reference's target engine does), else on the device of
+    ``source`` (a push), on that device's current stream, and returns before it completes.
+    ``engine="sm"``: one kernel streams 16-byte vectors over NVLink (ids staged to the device);
+    ``engine="dma"``: the copy engines, one transfer per run of blocks adjacent on both sides.
+    """
+    s_ptr, s_n, s_bb, s_dev = _pool(source, "source")
+    t_ptr, t_n, t_bb, t_dev = _pool(target, "target")
+    if s_bb != t_bb:
+        raise ValueError(f"block sizes differ: source {s_bb} bytes, target {t_bb} bytes")
+    dev = t_dev if t_dev is not None else s_dev
+    if dev is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    if engine == "dma":
+        src = _ids_array(source_block_ids, "source_block_ids")
+        dst = _ids_array(target_block_ids, "target_block_ids")
+        if src.shape != dst.shape:
+            raise ValueError(f"{src.size} source ids but {dst.size} target ids")
+        if src.size == 0:
+            return
+        with torch.cuda.device(dev):
+            st = lib.aeg_migrate_blocks_dma(t_ptr, t_n, s_ptr, s_n, s_bb, src.ctypes.data, dst.ctypes.data,
+                                            src.size, _stream(dev))
+        check(st, "migrate_blocks_dma")
+        return
+    if engine != "sm":
+        raise ValueError(f"engine must be 'sm' or 'dma', not {engine!r}")
+    src = _device_ids(source_block_ids, dev, "source_block_ids")
+    dst = _device_ids(target_block_ids, dev, "target_block_ids")
+    if src.numel() != dst.numel():
+        raise ValueError(f"{src.numel()} source ids but {dst.numel()} target ids")
+    if src.numel() == 0:
+        return
+    with torch.cuda.device(dev):
+        st = lib.aeg_migrate_blocks(t_ptr, t_n, s_ptr, s_n, s_bb, src.data_ptr(), dst.data_ptr(), src.numel(),
+                                    _stream(dev))
+    check(st, "migrate_blocks")
+    src.record_stream(torch.cuda.current_stream(dev))
+    dst.record_stream(torch.cuda.current_stream(dev))
+
+
+# --------------------------------------------------------------------------------------------
 # Per-layer cache write
 
 

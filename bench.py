@@ -42,7 +42,7 @@ def _args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate"])
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--unfused", action="store_true",
@@ -50,7 +50,7 @@ def _args():
     p.add_argument("--compact-pool", action="store_true",
                    help="size the block pool to the blocks the batch uses (same kernels; small-case profiling)")
     p.add_argument("--scale", type=float, default=1.0,
-                   help="cfg5 only: scale the pool, swap and copy sizes (small cases for profiling)")
+                   help="cfg5 / migrate only: scale the pool and the moved block counts (small cases)")
     p.add_argument("--profile-run", action="store_true",
                    help="timed graph replays only: no clock pre-roll, per-launch timing, end-to-end or CPU leg")
     return p.parse_args()
@@ -532,6 +532,96 @@ def run_swap(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_migrate(args, world, rank, local):
+    """GPU <-> GPU block migration over NVLink (GB/s): every rank pulls the cfg5 swap set (4096
+    scattered 917,504-byte blocks) from the pool of rank (r + 1) % N, mapped through its IPC
+    handle, into scattered blocks of its own pool, all ranks at once (each GPU's links carry
+    data both ways). Also timed: the copy-engine form, a push, and one contiguous 1 GiB
+    copy-engine transfer from the peer (the link reference)."""
+    from aegaeon_b200 import layout, ops, synth
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world < 2:
+        if rank == 0:
+            print(json.dumps({"metric": "KV-block migration GB/s", "n_gpus": world,
+                              "unavailable": "GPU <-> GPU migration needs two or more GPUs (torchrun)"}), flush=True)
+        return
+    c = dict(synth.SWAP_CFG)
+    if args.scale != 1.0:
+        for k in ("device_blocks", "swap_blocks"):
+            c[k] = max(2, int(c[k] * args.scale))
+        c["swap_blocks"] = min(c["swap_blocks"], c["device_blocks"])
+    shape = (c["device_blocks"],) + layout.kv_block_shape(c["num_layers"], c["num_kv_heads"], c["head_dim"])
+    kv = torch.empty(shape, dtype=c["dtype"], device=device)
+    synth.random_bits_(kv, c["seed"] + rank)
+    bb = layout.block_bytes(kv)
+    handles = [None] * world
+    torch.distributed.all_gather_object(handles, (ops.export_kv_cache(kv), kv.size(0), bb))
+    peer_rank = (rank + 1) % world
+    peer = ops.open_kv_cache(*handles[peer_rank])
+    g = torch.Generator().manual_seed(c["seed"] + 100 + rank)
+    n = c["swap_blocks"]
+    src = torch.randperm(c["device_blocks"], generator=g)[:n]
+    dst = torch.randperm(c["device_blocks"], generator=g)[:n]
+    d_src, d_dst = src.to(device), dst.to(device)
+    run_len = max(1, min(c["device_blocks"], (1 << 30) // bb))
+    contiguous = torch.arange(run_len, dtype=torch.int64)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, reps):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(device)
+        _barrier(world)
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        t = torch.tensor([a.elapsed_time(b) / reps], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)  # slowest rank
+        return float(t.item())
+
+    reps = max(1, min(args.steps, 20))
+    res = {
+        "pull_sm_ms": timed(lambda: ops.migrate_blocks(d_src, d_dst, peer, kv), reps),
+        "pull_dma_ms": timed(lambda: ops.migrate_blocks(src, dst, peer, kv, engine="dma"), reps),
+        "push_sm_ms": timed(lambda: ops.migrate_blocks(d_dst, d_src, kv, peer), reps),
+        "link_contiguous_dma_ms": timed(lambda: ops.migrate_blocks(contiguous, contiguous, peer, kv, engine="dma"),
+                                        reps),
+    }
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    peer.close()
+    _barrier(world)
+    per_gpu = {k.replace("_ms", "_gbs"): (run_len if k.startswith("link") else n) * bb / (v / 1e3) / 1e9
+               for k, v in res.items()}
+    link = per_gpu["link_contiguous_dma_gbs"]
+    best = max(per_gpu["pull_sm_gbs"], per_gpu["pull_dma_gbs"])
+    if rank == 0:
+        line = {
+            "metric": "KV-block migration GB/s", "value": best * world, "unit": "GB/s", "n_gpus": world,
+            "steps": reps, "warmup": max(args.warmup, 3), "ms_per_step": min(res["pull_sm_ms"], res["pull_dma_ms"]),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u16",
+            "data": "synthetic random 16-bit patterns",
+            "config": {"workload": f"every rank pulls {n} scattered {bb:,}-byte blocks from rank (r + 1) % {world} "
+                                   f"(IPC-mapped pool of {c['device_blocks']} blocks) into scattered blocks of its own"
+                                   + ("" if args.scale == 1.0 else f" (scaled x{args.scale})")},
+            "per_gpu_gbs": per_gpu, "detail_ms": res,
+            "roofline": {"bound": "nvlink", "kernel": "block_copy_vec_kernel (migrate_blocks, pull over NVLink)",
+                         "achieved": per_gpu["pull_sm_gbs"], "peak": link, "unit": "GB/s",
+                         "frac": per_gpu["pull_sm_gbs"] / link,
+                         "peak_source": "measured here: one contiguous 1 GiB copy-engine transfer from the peer, "
+                                        "all ranks at once",
+                         "traffic": None},
+        }
+        print(json.dumps(line), flush=True)
+    del kv
+
+
 # ------------------------------------------------------------------------------------------
 # Reference arm: the CPU restatement of the reference's path on the host cores
 
@@ -541,6 +631,11 @@ def run_reference(args, world, rank):
         return
     from aegaeon_b200 import synth
 
+    if args.config == "migrate":
+        print(json.dumps({"impl": "reference", "metric": "KV-block migration GB/s",
+                          "unavailable": "the reference's GPU -> GPU migration is a stub (Worker.migrate_blocks "
+                                         "raises NotImplementedError, aegaeon/aegaeon/worker.py:851)"}), flush=True)
+        return
     name = args.config if args.config != "cfg5" else "cfg2"
     cfg = synth.CONFIGS[name]
     lay = synth.make_layout(cfg)
@@ -595,6 +690,8 @@ def main():
         if args.config == "cfg5":
             if rank == 0:
                 run_swap(args, world, rank, local)
+        elif args.config == "migrate":
+            run_migrate(args, world, rank, local)
         else:
             run_decode(args, world, rank, local)
     finally:

@@ -1,7 +1,7 @@
 /*
  * aegaeon_b200 — C ABI of the B200-native per-token serving path of Aegaeon.
  *
- * The library replaces four operations of the reference serving path:
+ * The library replaces these operations of the reference serving path:
  *
  *   aeg_swap               aegaeon/ops/swap.cu:25-60 (declared aegaeon/ops/ops.h:4-10,
  *                          bound to Python at aegaeon/ops/ops.cpp:4-5 as `aegaeon.ops.swap`)
@@ -10,6 +10,8 @@
  *                          and aegaeon/aegaeon/worker.py:841-858 would call)
  *   aeg_reshape_and_cache  vLLM 0.5.1 `_C_cache_ops.reshape_and_cache_flash`, reached per layer
  *                          from the model forward at aegaeon/aegaeon/worker.py:517-523
+ *   aeg_migrate_blocks     the GPU->GPU migration the reference stubs (worker.py:841-872), with
+ *   aeg_ipc_export/open    the KV-cache IPC handle exchange it plans (cuda_wrapper.py:77-104)
  *   aeg_decode_plan +      vLLM 0.5.1 FlashAttention backend decode call
  *   aeg_paged_attn_decode  `flash_attn_with_kvcache(q, K_l, V_l, block_table, cache_seqlens, ...)`
  *                          with the metadata built at aegaeon/aegaeon/worker.py:554-713
@@ -111,6 +113,53 @@ AEG_API int aeg_swap_sm(void* dev_pool, void* host_pool, size_t block_bytes, int
  */
 AEG_API int aeg_copy_blocks(void* pool, size_t block_bytes, int64_t num_blocks, const int64_t* d_src_ids,
                     const int64_t* d_dst_ids, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * f1. GPU <-> GPU KV block migration over NVLink. Replaces the reference's stubbed migration
+ * path: Worker.register_kvcache_mem_handles / Worker.migrate_blocks
+ * (aegaeon/aegaeon/worker.py:841-872) and BlockManager._migrate_requests
+ * (aegaeon/aegaeon/block_manager.py:876-950), which hand the target engine the source
+ * engine's KV-cache CUDA IPC handles (aegaeon/aegaeon/cuda_wrapper.py:77-104, 190-208:
+ * cudaIpcGetMemHandle / cudaIpcOpenMemHandle with lazy peer access) so that the target pulls
+ * a request's blocks into blocks of its own pool.
+ *
+ * An AEG_IPC_HANDLE_BYTES-byte handle names a device pool of the exporting process: the CUDA
+ * IPC handle of the allocation that holds it, the pool's offset in that allocation and the
+ * allocation's size (so the importer can range-check). Handles are plain bytes: send them
+ * through any host channel (a torch.distributed store, a pipe).
+ */
+#define AEG_IPC_HANDLE_BYTES 96
+
+/* Fills `handle_out` (AEG_IPC_HANDLE_BYTES bytes) for the device pool at `dev_pool`, which
+ * must lie in memory from cudaMalloc (e.g. a tensor of PyTorch's default allocator). */
+AEG_API int aeg_ipc_export(const void* dev_pool, void* handle_out);
+
+/* Maps the pool named by `handle` (exported by another process) into this process and stores
+ * its address in *dev_pool_out; *pool_bytes_out (may be NULL) receives the bytes from that
+ * address to the end of the exporter's allocation. Opening a handle that this process has
+ * already opened returns the same mapping (reference counted). */
+AEG_API int aeg_ipc_open(const void* handle, void** dev_pool_out, int64_t* pool_bytes_out);
+
+/* Releases a mapping returned by aeg_ipc_open (after work that reads it has completed). */
+AEG_API int aeg_ipc_close(void* dev_pool);
+
+/* For i < n: dst_pool[d_dst_ids[i]] <- src_pool[d_src_ids[i]] (block_bytes each), by a kernel
+ * on the current device. One pool is normally this GPU's and the other a peer GPU's (mapped by
+ * aeg_ipc_open, or a peer allocation of this process): the kernel pulls (peer source) or pushes
+ * (peer target) 16-byte vectors over NVLink. Before any launch the host checks that both pools
+ * are device memory that the current device can address (peer access is enabled when needed)
+ * and that [pool, pool + num_blocks * block_bytes) lies inside each pool's allocation.
+ * `d_src_ids`/`d_dst_ids` are DEVICE int64 arrays on the current device; ids out of range are
+ * skipped and raise AEG_DEVERR_BLOCK_ID_RANGE. Target blocks must be distinct. */
+AEG_API int aeg_migrate_blocks(void* dst_pool, int64_t n_dst_blocks, const void* src_pool,
+                               int64_t n_src_blocks, size_t block_bytes, const int64_t* d_src_ids,
+                               const int64_t* d_dst_ids, int64_t n, void* stream);
+
+/* Copy-engine form of aeg_migrate_blocks: HOST id arrays, every id range-checked before anything
+ * is enqueued, one cudaMemcpyAsync per run of blocks adjacent on both sides. */
+AEG_API int aeg_migrate_blocks_dma(void* dst_pool, int64_t n_dst_blocks, const void* src_pool,
+                                   int64_t n_src_blocks, size_t block_bytes, const int64_t* src_ids,
+                                   const int64_t* dst_ids, int64_t n, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * a6. reshape_and_cache — replaces vLLM 0.5.1 `reshape_and_cache_flash(key, value, key_cache,

@@ -129,3 +129,43 @@ def test_ops_module_imports_and_fails_loudly_without_cuda():
         ops.copy_blocks([0], [1], kv)
     with pytest.raises(ValueError, match="CUDA"):
         ops.swap([0], [1], False, kv, torch.zeros_like(kv))
+
+
+def test_migration_and_ipc_validation_on_host():
+    lib = _native.lib
+    p, _k1 = _fake()
+    q, _k2 = _fake()
+    inval = _native.AEG_ERR_INVALID_ARGUMENT
+    ids = np.array([0, 1], np.int64)
+    assert lib.aeg_migrate_blocks(p, 8, q, 8, 64, ids.ctypes.data, ids.ctypes.data, 0, None) == 0
+    assert lib.aeg_migrate_blocks(p, 8, q, 8, 64, ids.ctypes.data, ids.ctypes.data, -1, None) == inval
+    assert lib.aeg_migrate_blocks(None, 8, q, 8, 64, ids.ctypes.data, ids.ctypes.data, 2, None) == inval
+    assert lib.aeg_migrate_blocks(p, 8, q, 8, 0, ids.ctypes.data, ids.ctypes.data, 2, None) == inval
+    assert lib.aeg_migrate_blocks(p, 8, q, 8, 64, None, ids.ctypes.data, 2, None) == inval
+    # copy-engine form: every host id is range-checked before anything is enqueued
+    bad = np.array([0, 8], np.int64)
+    assert lib.aeg_migrate_blocks_dma(p, 8, q, 8, 64, bad.ctypes.data, ids.ctypes.data, 2, None) == inval
+    assert b"source block id 8" in lib.aeg_last_error()
+    assert lib.aeg_migrate_blocks_dma(p, 8, q, 8, 64, ids.ctypes.data, bad.ctypes.data, 2, None) == inval
+    assert b"target block id 8" in lib.aeg_last_error()
+    # IPC handles: only this library's handles are accepted; unknown mappings cannot be closed
+    out = ctypes.c_void_p()
+    assert lib.aeg_ipc_open(b"\0" * _native.AEG_IPC_HANDLE_BYTES, ctypes.byref(out), None) == inval
+    assert lib.aeg_ipc_close(p) == inval
+    assert lib.aeg_ipc_export(None, ctypes.create_string_buffer(_native.AEG_IPC_HANDLE_BYTES)) == inval
+
+
+def test_migration_ops_fail_loudly_without_cuda():
+    import torch
+
+    from aegaeon_b200 import ops
+
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only check")
+    kv = torch.zeros((4, 1, 2, 16, 4, 128), dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.migrate_blocks([0], [1], kv, kv)
+    with pytest.raises(ValueError, match="IPC handle"):
+        ops.open_kv_cache(b"short", 4, 1024)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.export_kv_cache(kv)
