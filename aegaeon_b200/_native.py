@@ -47,6 +47,9 @@ SIGNATURES = {
     "aeg_ipc_close": (_i32, [_c_void_p]),
     "aeg_migrate_blocks": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "aeg_migrate_blocks_dma": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "aeg_prepare_step_inputs": (_i32, [_c_void_p, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i64,
+                                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "aeg_update_block_tables": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i64, _c_void_p]),
     "aeg_reshape_and_cache": (_i32, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64,
                                      _c_void_p, _i64, _i32, _i32, _c_void_p]),
     "aeg_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),

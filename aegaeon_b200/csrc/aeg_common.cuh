@@ -59,6 +59,7 @@ int launch_block_copy(const void* src_pool, void* dst_pool, size_t block_bytes, 
 uint32_t deverr_read_and_clear_copy(cudaStream_t s, cudaError_t* err);
 uint32_t deverr_read_and_clear_cache(cudaStream_t s, cudaError_t* err);
 uint32_t deverr_read_and_clear_attn(cudaStream_t s, cudaError_t* err);
+uint32_t deverr_read_and_clear_step(cudaStream_t s, cudaError_t* err);
 
 // ---------------------------------------------------------------------------------------
 // Device helpers.

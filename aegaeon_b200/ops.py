@@ -273,6 +273,76 @@ def migrate_blocks(source_block_ids, target_block_ids, source, target, *, engine
 
 
 # --------------------------------------------------------------------------------------------
+# Per-step model inputs on the device (Worker._prepare_model_inputs, aegaeon/aegaeon/worker.py:596-682)
+
+
+class StepInputs:
+    """Device tensors of one step's model inputs (see ``prepare_step_inputs``)."""
+
+    def __init__(self, B: int, table_stride: int, capacity: int, device: torch.device):
+        self.capacity = int(capacity)
+        self.slot_mapping = torch.empty(self.capacity, dtype=torch.int64, device=device)
+        self.positions = torch.empty(self.capacity, dtype=torch.int64, device=device)
+        self.query_lens = torch.empty(B, dtype=torch.int64, device=device)
+        self.query_start_loc = torch.empty(B + 1, dtype=torch.int32, device=device)
+        self.seq_start_loc = torch.empty(B + 1, dtype=torch.int32, device=device)
+        self.block_tables = torch.empty((B, table_stride), dtype=torch.int32, device=device)
+        self.num_tokens = torch.empty(1, dtype=torch.int64, device=device)
+
+
+def prepare_step_inputs(block_tables: torch.Tensor, context_lens: torch.Tensor, seq_lens: torch.Tensor,
+                        capacity: int | None = None, out: StepInputs | None = None) -> StepInputs:
+    """Slot mapping, positions, start offsets and attention table rows of a step, on the device.
+
+    ``block_tables`` (int32 [B, W], request i's blocks in row i), ``context_lens`` and ``seq_lens``
+    (int32 [B]) are device tensors that stay resident across steps (``update_block_tables`` applies
+    a step's new blocks). ``capacity`` bounds the new tokens written (default B, i.e. a decode
+    batch); ``out.num_tokens`` holds the true count, and a larger count raises a device error.
+    Runs on the current stream; nothing is copied to the host.
+    """
+    for t, name in ((block_tables, "block_tables"), (context_lens, "context_lens"), (seq_lens, "seq_lens")):
+        _require_cuda(t, name)
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    if block_tables.dim() != 2:
+        raise ValueError("block_tables must be [B, W]")
+    B, W = block_tables.shape
+    if context_lens.numel() != B or seq_lens.numel() != B:
+        raise ValueError("context_lens and seq_lens must have one entry per table row")
+    dev = block_tables.device
+    if out is None:
+        out = StepInputs(B, W, B if capacity is None else capacity, dev)
+    with torch.cuda.device(dev):
+        st = lib.aeg_prepare_step_inputs(block_tables.data_ptr(), W, context_lens.data_ptr(), seq_lens.data_ptr(), B,
+                                         out.slot_mapping.data_ptr(), out.positions.data_ptr(), out.capacity,
+                                         out.query_lens.data_ptr(), out.query_start_loc.data_ptr(),
+                                         out.seq_start_loc.data_ptr(), out.block_tables.data_ptr(),
+                                         out.num_tokens.data_ptr(), _stream(dev))
+    check(st, "prepare_step_inputs")
+    return out
+
+
+def update_block_tables(block_tables: torch.Tensor, updates) -> None:
+    """Writes ``block_tables[row, col] = block`` for every (row, col, block) triple of ``updates``
+    (an int32 [n, 3] tensor or a sequence of triples), on the current stream."""
+    _require_cuda(block_tables, "block_tables")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or not block_tables.is_contiguous():
+        raise ValueError("block_tables must be a contiguous int32 [rows, W] tensor")
+    dev = block_tables.device
+    if isinstance(updates, torch.Tensor):
+        u = updates.to(device=dev, dtype=torch.int32).contiguous().view(-1, 3)
+    else:
+        u = torch.as_tensor(np.asarray(updates, dtype=np.int32).reshape(-1, 3)).to(dev, non_blocking=True)
+    if u.numel() == 0:
+        return
+    with torch.cuda.device(dev):
+        st = lib.aeg_update_block_tables(block_tables.data_ptr(), block_tables.size(1), block_tables.size(0),
+                                         u.data_ptr(), u.size(0), _stream(dev))
+    check(st, "update_block_tables")
+    u.record_stream(torch.cuda.current_stream(dev))
+
+
+# --------------------------------------------------------------------------------------------
 # Per-layer cache write
 
 

@@ -42,7 +42,7 @@ def _args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate"])
+    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate", "prep"])
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--unfused", action="store_true",
@@ -622,6 +622,89 @@ def run_migrate(args, world, rank, local):
     del kv
 
 
+def _prep_batches():
+    """(name, seq_lens, context_lens, block lists) of the step-input benchmark: the cfg2 and cfg3
+    decode batches and a mixed batch of 32 prompts (lognormal lengths) with 224 decode requests."""
+    from aegaeon_b200 import synth
+
+    out = []
+    for name in ("cfg2", "cfg3"):
+        lay = synth.make_layout(synth.CONFIGS[name])
+        seq = lay.seq_lens.astype(np.int64)
+        nb = (seq + 15) // 16
+        tables = [lay.block_tables[i, :nb[i]].tolist() for i in range(len(seq))]
+        out.append((f"{name} decode (B={len(seq)})", seq.tolist(), (seq - 1).tolist(), tables))
+    rng = np.random.default_rng(5)
+    seq = np.clip(np.round(rng.lognormal(6, 1, 256)), 4, 4096).astype(np.int64)
+    ctx = np.where(np.arange(256) < 32, 0, seq - 1)
+    perm = rng.permutation(1 << 20)
+    tables, off = [], 0
+    for n in seq:
+        k = int((n + 15) // 16)
+        tables.append(perm[off:off + k].tolist())
+        off += k
+    out.append(("mixed: 32 prompts + 224 decode", seq.tolist(), ctx.tolist(), tables))
+    return out
+
+
+def run_prep(args, world, rank, local):
+    """Per-step model inputs on the device (ops.prepare_step_inputs) against the reference's
+    per-request Python loops restated in the oracle (Worker._prepare_model_inputs,
+    aegaeon/aegaeon/worker.py:596-682), per batch: device microseconds per step (CUDA events,
+    inputs resident) and the host loop's microseconds."""
+    from aegaeon_b200 import ops
+    from oracle import oracle as orc
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    rows = {}
+    for name, seq, ctx, tables in _prep_batches():
+        B = len(seq)
+        W = max(len(t) for t in tables)
+        t = np.zeros((B, W), np.int32)
+        for i, r in enumerate(tables):
+            t[i, :len(r)] = r
+        bt = torch.as_tensor(t, device=device)
+        c = torch.as_tensor(np.asarray(ctx, np.int32), device=device)
+        s = torch.as_tensor(np.asarray(seq, np.int32), device=device)
+        T = int(sum(a - b for a, b in zip(seq, ctx)))
+        out = ops.StepInputs(B, W, T, device)
+        for _ in range(max(args.warmup, 3)):
+            ops.prepare_step_inputs(bt, c, s, out=out)
+        torch.cuda.synchronize(device)
+        reps = 200
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            ops.prepare_step_inputs(bt, c, s, out=out)
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        dev_us = a.elapsed_time(b) / reps * 1e3
+        want = orc.np_step_inputs(seq, ctx, tables)
+        ok = out.slot_mapping[:T].cpu().numpy().tolist() == want["slot_mapping"].tolist()
+        t0 = time.perf_counter()
+        n_host = 0
+        while time.perf_counter() - t0 < 1.0:
+            orc.np_step_inputs(seq, ctx, tables)
+            n_host += 1
+        host_us = (time.perf_counter() - t0) / n_host * 1e6
+        rows[name] = {"tokens": T, "device_us": dev_us, "host_loop_us": host_us, "matches_oracle": ok}
+    if rank == 0:
+        first = rows[next(iter(rows))]
+        print(json.dumps({
+            "metric": "step-input prep us", "value": first["device_us"], "unit": "us", "n_gpus": 1, "steps": 200,
+            "warmup": max(args.warmup, 3), "ms_per_step": first["device_us"] / 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int32/int64", "data": "synthetic (bench configs)",
+            "config": {"workload": "slot mapping, positions, start offsets and attention table rows of one step; "
+                                   "value = the cfg2 decode batch"},
+            "batches": rows,
+            "cpu_baseline": {"value": first["host_loop_us"], "unit": "us", "cores": 1, "kind": "port",
+                             "sample": "the oracle's restatement of the reference's per-request Python loops "
+                                       "(no tensor creation or host-to-device copies), timed for 1 s"},
+        }), flush=True)
+
+
 # ------------------------------------------------------------------------------------------
 # Reference arm: the CPU restatement of the reference's path on the host cores
 
@@ -631,6 +714,11 @@ def run_reference(args, world, rank):
         return
     from aegaeon_b200 import synth
 
+    if args.config == "prep":
+        print(json.dumps({"impl": "reference", "metric": "step-input prep us",
+                          "unavailable": "the reference builds step inputs in Python inside Worker (ray, vLLM); "
+                                         "its loop is timed as the cpu_baseline of --config prep"}), flush=True)
+        return
     if args.config == "migrate":
         print(json.dumps({"impl": "reference", "metric": "KV-block migration GB/s",
                           "unavailable": "the reference's GPU -> GPU migration is a stub (Worker.migrate_blocks "
@@ -692,6 +780,9 @@ def main():
                 run_swap(args, world, rank, local)
         elif args.config == "migrate":
             run_migrate(args, world, rank, local)
+        elif args.config == "prep":
+            if rank == 0:
+                run_prep(args, world, rank, local)
         else:
             run_decode(args, world, rank, local)
     finally:

@@ -12,6 +12,8 @@
  *                          from the model forward at aegaeon/aegaeon/worker.py:517-523
  *   aeg_migrate_blocks     the GPU->GPU migration the reference stubs (worker.py:841-872), with
  *   aeg_ipc_export/open    the KV-cache IPC handle exchange it plans (cuda_wrapper.py:77-104)
+ *   aeg_prepare_step_inputs the per-step Python loops of Worker._prepare_model_inputs
+ *                          (worker.py:596-682), on the device
  *   aeg_decode_plan +      vLLM 0.5.1 FlashAttention backend decode call
  *   aeg_paged_attn_decode  `flash_attn_with_kvcache(q, K_l, V_l, block_table, cache_seqlens, ...)`
  *                          with the metadata built at aegaeon/aegaeon/worker.py:554-713
@@ -160,6 +162,40 @@ AEG_API int aeg_migrate_blocks(void* dst_pool, int64_t n_dst_blocks, const void*
 AEG_API int aeg_migrate_blocks_dma(void* dst_pool, int64_t n_dst_blocks, const void* src_pool,
                                    int64_t n_src_blocks, size_t block_bytes, const int64_t* src_ids,
                                    const int64_t* dst_ids, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * f4. Per-step model inputs on the device. Replaces the Python loops of
+ * Worker._prepare_model_inputs (aegaeon/aegaeon/worker.py:596-682; padding utils.py:241-257)
+ * for a batch whose block tables stay resident on the device between steps.
+ *
+ * Inputs (DEVICE): block_tables int32 [B, table_stride], row i holding request i's blocks in
+ * order; context_lens, seq_lens int32 [B] (tokens already cached / after this step).
+ * Outputs (DEVICE), for the T = sum(seq_len - context_len) new tokens in request order:
+ *   slot_mapping, positions  int64 [capacity]: position p of request i and its slot
+ *                            block_tables[i][p / 16] * 16 + p % 16 (worker.py:612-633)
+ *   query_lens               int64 [B]      seq_len - context_len
+ *   query_start_loc          int32 [B + 1]  exclusive cumulative sums of query_lens / seq_lens
+ *   seq_start_loc            int32 [B + 1]  (worker.py:653-676)
+ *   attn_tables (or NULL)    int32 [B, table_stride]: the rows attention reads, as the reference
+ *                            builds them (worker.py:603-609, 640-646): a decode request's
+ *                            ceil(seq_len / 16) blocks then zeros, a prompt's row all zeros
+ *   num_tokens               int64 [1]      T
+ * A request with context_len < 0, seq_len < context_len or seq_len > 16 * table_stride gets no new
+ * tokens and raises AEG_DEVERR_SEQ_LEN_RANGE; when T > capacity the tokens past capacity are not
+ * written and AEG_DEVERR_SLOT_RANGE is raised (num_tokens still holds T). Two launches. */
+AEG_API int aeg_prepare_step_inputs(const int32_t* block_tables, int table_stride,
+                                    const int32_t* context_lens, const int32_t* seq_lens, int B,
+                                    int64_t* slot_mapping, int64_t* positions, int64_t capacity,
+                                    int64_t* query_lens, int32_t* query_start_loc,
+                                    int32_t* seq_start_loc, int32_t* attn_tables,
+                                    int64_t* num_tokens, void* stream);
+
+/* Applies n updates to the DEVICE tables [rows, table_stride]: d_updates is a DEVICE int32 array
+ * of (row, column, block id) triples (the blocks a step appended or a new request's row).
+ * Triples outside the table are skipped and raise AEG_DEVERR_BLOCK_ID_RANGE. Updates to one
+ * cell within a call land in an unspecified order. */
+AEG_API int aeg_update_block_tables(int32_t* block_tables, int table_stride, int rows,
+                                    const int32_t* d_updates, int64_t n, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * a6. reshape_and_cache — replaces vLLM 0.5.1 `reshape_and_cache_flash(key, value, key_cache,

@@ -21,6 +21,7 @@ Reference anchors (paths inside the reference checkout):
                      causal, one query token); GQA head map h // (Hq / Hkv); tables/lengths from
                      worker.py:640-653; layout worker.py:388-451, config.py:256-271
   slot mapping       aegaeon/aegaeon/worker.py:596-682; padding aegaeon/aegaeon/utils.py:241-257
+  step inputs        the same function: positions, offsets, decode/prompt table rows (np_step_inputs)
 
 Parity pins: the reference ships no kernel tests or golden vectors (its tests are smoke scripts
 without numeric assertions). ``swap`` is pinned against the reference's own operator compiled
@@ -192,6 +193,38 @@ def np_slot_mapping(seq_lens, context_lens, tables) -> np.ndarray:
         for i in range(c, n):
             slots.append(int(t[i // 16]) * 16 + i % 16)
     return np.asarray(slots, dtype=np.int64)
+
+
+def np_step_inputs(seq_lens, context_lens, tables) -> dict:
+    """Per-step model inputs of a batch, restated from Worker._prepare_model_inputs
+    (aegaeon/aegaeon/worker.py:596-682; padding utils.py:241-257).
+
+    ``tables[i]`` is request i's block list. Per request (worker.py:596-633): a decode request
+    (context_len > 0) keeps its block list as its table row, a prompt gets an empty row;
+    positions context_len .. seq_len - 1 and their slots table[p // 16] * 16 + p % 16 are
+    appended in request order. Rows are zero-padded to the longest (worker.py:640-646); query
+    and sequence start offsets are int32 cumulative sums with a leading 0 (worker.py:653-676).
+    """
+    rows, positions, slots, query_lens = [], [], [], []
+    for n, c, t in zip(seq_lens, context_lens, tables):
+        rows.append(list(t) if c > 0 else [])
+        query_lens.append(n - c)
+        for p in range(c, n):
+            positions.append(p)
+            slots.append(int(t[p // 16]) * 16 + p % 16)
+    width = max((len(r) for r in rows), default=0)
+    padded = np.zeros((len(rows), width), dtype=np.int32)
+    for i, r in enumerate(rows):
+        padded[i, :len(r)] = r
+    q = np.asarray(query_lens, dtype=np.int64)
+    n = np.asarray(seq_lens, dtype=np.int64)
+    qsl = np.zeros(len(q) + 1, dtype=np.int32)
+    ssl = np.zeros(len(n) + 1, dtype=np.int32)
+    qsl[1:] = np.cumsum(q).astype(np.int32)
+    ssl[1:] = np.cumsum(n).astype(np.int32)
+    return {"slot_mapping": np.asarray(slots, dtype=np.int64), "positions": np.asarray(positions, dtype=np.int64),
+            "query_lens": q, "query_start_loc": qsl, "seq_start_loc": ssl, "block_tables": padded,
+            "seq_lens": np.asarray(seq_lens, dtype=np.int32), "context_lens": np.asarray(context_lens, dtype=np.int32)}
 
 
 def compare_attention(got: np.ndarray, want: np.ndarray, dtype: int, atol: float = 2e-3, rtol: float = 1e-2):
