@@ -6,10 +6,13 @@
 // the block-table row of decode requests and an empty row for prompts (worker.py:603-609),
 // pads the rows with zeros (worker.py:640-646, utils.py:241-257) and builds query/sequence
 // start offsets by cumulative sums (worker.py:653-676). Here:
-//   * step_scan_kernel (one CTA): query lengths, both start-offset arrays and the token count;
-//   * step_expand_kernel (grid): for every new token its request (binary search over the
-//     query start offsets), position and slot; and the attention table rows (a decode row is
-//     the request's row, a prompt row zeros);
+//   * step_fused_kernel (batches of up to kFusedMaxB requests, one launch): every CTA scans the
+//     batch's lengths into query start offsets in shared memory (CTA 0 also writes the offset
+//     arrays, query lengths and token count), then takes its share of the new tokens: request
+//     of the token by binary search in shared memory, position and slot; and its share of the
+//     attention table rows (a decode row is the request's blocks, a prompt row zeros);
+//   * step_scan_kernel + step_expand_kernel: the same in two launches for larger batches (one
+//     CTA scans into global memory, the grid expands);
 //   * table_update_kernel: applies (row, column, block id) deltas to the persistent tables, so
 //     that a step uploads the blocks that changed instead of the whole padded table.
 // Integer work, bit-exact with the reference's arithmetic.
@@ -27,6 +30,10 @@ constexpr int kScanThreads = 1024;
 constexpr int kExpandThreads = 256;
 
 // Length of request i's new-token range, 0 (and a device error) for an invalid request.
+__device__ __forceinline__ bool request_ok(int c, int n, int table_stride) {
+  return c >= 0 && n >= c && static_cast<int64_t>(n) <= static_cast<int64_t>(table_stride) * kBlockTokens;
+}
+
 __device__ __forceinline__ int new_tokens(int c, int n, int table_stride) {
   if (c < 0 || n < c || static_cast<int64_t>(n) > static_cast<int64_t>(table_stride) * kBlockTokens) {
     atomicOr(&g_deverr_step, AEG_DEVERR_SEQ_LEN_RANGE);
@@ -126,6 +133,103 @@ step_expand_kernel(const int32_t* __restrict__ tables, int table_stride, const i
   }
 }
 
+constexpr int kFusedThreads = 512;
+constexpr int kFusedMaxB = 8192;
+
+__global__ void __launch_bounds__(kFusedThreads)
+step_fused_kernel(const int32_t* __restrict__ tables, int table_stride, const int32_t* __restrict__ context_lens,
+                  const int32_t* __restrict__ seq_lens, int B, int64_t* __restrict__ slot_mapping,
+                  int64_t* __restrict__ positions, int64_t capacity, int64_t* __restrict__ query_lens,
+                  int32_t* __restrict__ query_start_loc, int32_t* __restrict__ seq_start_loc,
+                  int32_t* __restrict__ attn_tables, int64_t* __restrict__ num_tokens) {
+  __shared__ int32_t s_start[kFusedMaxB + 1];  // query start offsets (wrapped to int32 like the reference)
+  __shared__ int64_t s_q[kFusedThreads / 32], s_s[kFusedThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const bool lead = blockIdx.x == 0;
+  const int per = (B + kFusedThreads - 1) / kFusedThreads;
+  const int i0 = min(B, tid * per), i1 = min(B, i0 + per);
+  int64_t q = 0, sl = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int c = context_lens[i], n = seq_lens[i];
+    const bool ok = request_ok(c, n, table_stride);
+    if (!ok && lead) atomicOr(&g_deverr_step, AEG_DEVERR_SEQ_LEN_RANGE);
+    q += ok ? n - c : 0;
+    sl += n;
+  }
+  int64_t qi = q, si = sl;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t tq = __shfl_up_sync(0xffffffffu, qi, o), ts = __shfl_up_sync(0xffffffffu, si, o);
+    if (lane >= o) {
+      qi += tq;
+      si += ts;
+    }
+  }
+  if (lane == 31) {
+    s_q[wid] = qi;
+    s_s[wid] = si;
+  }
+  __syncthreads();
+  int64_t qo = 0, so = 0, T = 0, S = 0;
+  for (int w = 0; w < kFusedThreads / 32; ++w) {
+    if (w < wid) {
+      qo += s_q[w];
+      so += s_s[w];
+    }
+    T += s_q[w];
+    S += s_s[w];
+  }
+  qo += qi - q;
+  so += si - sl;
+  for (int i = i0; i < i1; ++i) {
+    const int c = context_lens[i], n = seq_lens[i];
+    const int len = request_ok(c, n, table_stride) ? n - c : 0;
+    s_start[i] = static_cast<int32_t>(qo);
+    if (lead) {
+      query_lens[i] = len;
+      query_start_loc[i] = static_cast<int32_t>(qo);
+      seq_start_loc[i] = static_cast<int32_t>(so);
+    }
+    qo += len;
+    so += n;
+  }
+  if (tid == 0) {
+    s_start[B] = static_cast<int32_t>(T);
+    if (lead) {
+      query_start_loc[B] = static_cast<int32_t>(T);
+      seq_start_loc[B] = static_cast<int32_t>(S);
+      *num_tokens = T;
+      if (T > capacity) atomicOr(&g_deverr_step, AEG_DEVERR_SLOT_RANGE);
+    }
+  }
+  __syncthreads();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid;
+  const int64_t Tw = T < capacity ? T : capacity;
+  for (int64_t t = first; t < Tw; t += stride) {
+    // start[lo] <= t < start[lo + 1] at the end (start[0] = 0, start[B] = T > t): request lo has
+    // new tokens even when others share its offset.
+    int lo = 0, hi = B;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (static_cast<int64_t>(static_cast<uint32_t>(s_start[mid])) <= t) lo = mid; else hi = mid;
+    }
+    const int64_t p = context_lens[lo] + (t - static_cast<int64_t>(static_cast<uint32_t>(s_start[lo])));
+    const int32_t blk = tables[static_cast<int64_t>(lo) * table_stride + p / kBlockTokens];
+    positions[t] = p;
+    slot_mapping[t] = static_cast<int64_t>(blk) * kBlockTokens + p % kBlockTokens;
+  }
+  if (attn_tables != nullptr) {
+    const int64_t cells = static_cast<int64_t>(B) * table_stride;
+    for (int64_t k = first; k < cells; k += stride) {
+      const int64_t i = k / table_stride, j = k - i * table_stride;
+      const int c = context_lens[i], n = seq_lens[i];
+      const int64_t used = (static_cast<int64_t>(n) + kBlockTokens - 1) / kBlockTokens;
+      attn_tables[k] = (c > 0 && request_ok(c, n, table_stride) && n > c && j < used) ? tables[k] : 0;
+    }
+  }
+}
+
 __global__ void table_update_kernel(int32_t* __restrict__ tables, int table_stride, int rows,
                                     const int32_t* __restrict__ updates, int64_t n) {
   for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
@@ -172,6 +276,16 @@ int aeg_prepare_step_inputs(const int32_t* block_tables, int table_stride, const
                     aeg::aligned(num_tokens, 8),
                 "prepare_step_inputs: int64 arrays must be 8-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (B <= aeg::kFusedMaxB) {
+    const int64_t work = std::max<int64_t>(capacity, attn_tables != nullptr ? static_cast<int64_t>(B) * table_stride : 0);
+    const int64_t want = std::max<int64_t>(1, (work + aeg::kFusedThreads - 1) / aeg::kFusedThreads);
+    const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(aeg::num_sms()) * 2));
+    aeg::step_fused_kernel<<<grid, aeg::kFusedThreads, 0, s>>>(block_tables, table_stride, context_lens, seq_lens, B,
+                                                              slot_mapping, positions, capacity, query_lens,
+                                                              query_start_loc, seq_start_loc, attn_tables, num_tokens);
+    AEG_CHECK_LAUNCH("prepare_step_inputs");
+    return AEG_OK;
+  }
   aeg::step_scan_kernel<<<1, aeg::kScanThreads, 0, s>>>(context_lens, seq_lens, B, table_stride, query_lens,
                                                         query_start_loc, seq_start_loc, num_tokens);
   AEG_CHECK_LAUNCH("prepare_step_inputs(scan)");

@@ -9,7 +9,7 @@ from oracle import oracle as orc
 
 def _batch(rng, B, prompt_frac=0.3, max_len=600):
     seq, ctx, tables = [], [], []
-    perm = rng.permutation(100000)
+    perm = rng.permutation(max(100000, B * ((max_len + 15) // 16)))
     off = 0
     for _ in range(B):
         n = int(rng.integers(1, max_len))

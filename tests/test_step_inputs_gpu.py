@@ -33,7 +33,7 @@ def _check(out, want, B, W):
     assert not got_t[:, w:].any()
 
 
-@pytest.mark.parametrize("B,prompt_frac", [(1, 0.0), (64, 0.0), (256, 0.0), (37, 0.4), (300, 1.0), (5000, 0.1)])
+@pytest.mark.parametrize("B,prompt_frac", [(1, 0.0), (64, 0.0), (256, 0.0), (37, 0.4), (300, 1.0), (5000, 0.1), (9000, 0.05)])
 def test_step_inputs_match_oracle(cuda_device, B, prompt_frac):
     rng = np.random.default_rng(B)
     seq, ctx, tables = _batch(rng, B, prompt_frac)
