@@ -29,6 +29,9 @@ AEG_DECODE_PREFETCH = 0x1
 
 AEG_IPC_HANDLE_BYTES = 96
 
+AEG_COPY_ENGINE_DMA = 0
+AEG_COPY_ENGINE_SM = 1
+
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
@@ -47,6 +50,9 @@ SIGNATURES = {
     "aeg_ipc_close": (_i32, [_c_void_p]),
     "aeg_migrate_blocks": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "aeg_migrate_blocks_dma": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "aeg_copy_segments_workspace_size": (_sz, [_i64]),
+    "aeg_copy_segments": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p, _sz,
+                                 _c_void_p]),
     "aeg_prepare_step_inputs": (_i32, [_c_void_p, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _i64,
                                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "aeg_update_block_tables": (_i32, [_c_void_p, _i32, _i32, _c_void_p, _i64, _c_void_p]),

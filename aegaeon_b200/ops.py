@@ -273,6 +273,62 @@ def migrate_blocks(source_block_ids, target_block_ids, source, target, *, engine
 
 
 # --------------------------------------------------------------------------------------------
+# Model-weight switch (aegaeon/aegaeon/worker.py:358-365: one copy_ per parameter)
+
+
+def copy_segments(dst: torch.Tensor, src: torch.Tensor, src_offsets, dst_offsets, sizes, *,
+                  engine: str = "dma") -> None:
+    """Copies byte segments ``src[src_offsets[i]:+sizes[i]] -> dst[dst_offsets[i]:+sizes[i]]``
+    between two storages in one call (offsets and sizes in bytes, relative to each tensor's
+    first byte), on the current stream of the CUDA side.
+
+    The weight-switch use: ``src`` the page-locked host model cache, ``dst`` the device weight
+    arena, one segment per parameter. ``engine="dma"``: copy engines, one transfer per run of
+    segments adjacent on both sides; ``engine="sm"``: one kernel through the mapped host memory.
+    Destination segments must not overlap; every segment must lie inside both tensors.
+    """
+    so, do, sz = (_ids_array(x, n) for x, n in ((src_offsets, "src_offsets"), (dst_offsets, "dst_offsets"),
+                                                (sizes, "sizes")))
+    if not (so.shape == do.shape == sz.shape):
+        raise ValueError("src_offsets, dst_offsets and sizes must have the same length")
+    if so.size == 0:
+        return
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("dst and src must be contiguous")
+    if (sz < 0).any() or (so < 0).any() or (do < 0).any():
+        raise ValueError("offsets and sizes must be non-negative")
+    if int((so + sz).max()) > src.numel() * src.element_size() or int((do + sz).max()) > dst.numel() * dst.element_size():
+        raise ValueError("a segment runs past the end of its tensor")
+    dev = dst.device if dst.device.type == "cuda" else src.device
+    if dev.type != "cuda":
+        raise ValueError("one of dst / src must be a CUDA tensor")
+    eng = {"dma": _native.AEG_COPY_ENGINE_DMA, "sm": _native.AEG_COPY_ENGINE_SM}.get(engine)
+    if eng is None:
+        raise ValueError(f"engine must be 'dma' or 'sm', not {engine!r}")
+    ws_bytes = lib.aeg_copy_segments_workspace_size(so.size) if eng == _native.AEG_COPY_ENGINE_SM else 0
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.aeg_copy_segments(dst.data_ptr(), src.data_ptr(), so.ctypes.data, do.ctypes.data, sz.ctypes.data,
+                                   so.size, eng, ws.data_ptr(), ws_bytes, _stream(dev))
+    check(st, "copy_segments")
+    ws.record_stream(torch.cuda.current_stream(dev))
+
+
+def tensor_segments(tensors, storage: torch.Tensor) -> tuple[np.ndarray, np.ndarray]:
+    """(byte offsets within ``storage``, byte sizes) of tensors that live inside ``storage``."""
+    base = storage.data_ptr()
+    end = base + storage.numel() * storage.element_size()
+    offs, sizes = [], []
+    for t in tensors:
+        n = t.numel() * t.element_size()
+        if not (base <= t.data_ptr() and t.data_ptr() + n <= end) or not t.is_contiguous():
+            raise ValueError("every tensor must be contiguous and inside the storage")
+        offs.append(t.data_ptr() - base)
+        sizes.append(n)
+    return np.asarray(offs, dtype=np.int64), np.asarray(sizes, dtype=np.int64)
+
+
+# --------------------------------------------------------------------------------------------
 # Per-step model inputs on the device (Worker._prepare_model_inputs, aegaeon/aegaeon/worker.py:596-682)
 
 

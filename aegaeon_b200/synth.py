@@ -180,3 +180,21 @@ def attention_flops_per_layer(cfg: DecodeConfig, layout: DecodeLayout) -> int:
 
 def default_scale(cfg: DecodeConfig) -> float:
     return 1.0 / math.sqrt(cfg.head_dim)
+
+
+def qwen2_7b_param_bytes(dtype_bytes: int = 2, layers: int = 28) -> list[int]:
+    """Byte sizes of Qwen2.5-7B's parameters in load order (hidden 3584, intermediate 18944,
+    28 query / 4 KV heads of 128, vocabulary 152064, untied embeddings): the weight-switch
+    workload."""
+    h, inter, kv, vocab = 3584, 18944, 4 * 128, 152064
+    shapes = [(vocab, h)]
+    for _ in range(layers):
+        shapes += [(h, h), (h,), (kv, h), (kv,), (kv, h), (kv,), (h, h), (inter, h), (inter, h), (h, inter), (h,), (h,)]
+    shapes += [(h,), (vocab, h)]
+    out = []
+    for sh in shapes:
+        n = 1
+        for d in sh:
+            n *= d
+        out.append(n * dtype_bytes)
+    return out

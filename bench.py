@@ -42,7 +42,7 @@ def _args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate", "prep"])
+    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate", "prep", "weights"])
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--unfused", action="store_true",
@@ -622,6 +622,91 @@ def run_migrate(args, world, rank, local):
     del kv
 
 
+def _weight_layout(scale: float):
+    """Parameter sizes of the weight-switch workload and their 16-byte-aligned packed offsets
+    (the layout of the reference's bump allocators, aegaeon/aegaeon/allocator.py:54-81)."""
+    from aegaeon_b200 import synth
+
+    layers = max(1, int(round(28 * scale)))
+    sizes = np.asarray(synth.qwen2_7b_param_bytes(2, layers), np.int64)
+    offs = np.zeros_like(sizes)
+    top = 0
+    for i, n in enumerate(sizes):
+        top = (top + 15) // 16 * 16
+        offs[i] = top
+        top += int(n)
+    return sizes, offs, top, layers
+
+
+def _time_calls(fn, reps, device, stream):
+    fn()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) / reps
+
+
+def _reference_weight_loop(arena, cache, offs, sizes):
+    """The reference's switch: one non-blocking copy_ per parameter (worker.py:358-365)."""
+    for o, n in zip(offs.tolist(), sizes.tolist()):
+        arena[o:o + n].copy_(cache[o:o + n], non_blocking=True)
+
+
+def run_weights(args, world, rank, local, reference_only=False):
+    """Model-weight switch (GB/s): Qwen2.5-7B's parameters (bf16) from a page-locked host model
+    cache into a device arena, one call (copy engines over runs of adjacent parameters, or one
+    kernel through the mapped host memory), against the reference's per-parameter copy_ loop
+    and a contiguous 1 GiB pinned copy (the host link)."""
+    from aegaeon_b200 import ops
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    sizes, offs, total, layers = _weight_layout(args.scale)
+    cache = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    cache[: 1 << 20].random_(0, 256)
+    arena = torch.empty(total, dtype=torch.uint8, device=device)
+    reps = max(1, min(args.steps, 3))
+    ref_ms = _time_calls(lambda: _reference_weight_loop(arena, cache, offs, sizes), reps, device, stream)
+    gb = total / 1e9
+    workload = (f"Qwen2.5-7B parameters ({len(sizes)} tensors, {layers} layers, bf16, {total / 1e9:.2f} GB) "
+                "pinned host model cache -> device arena, both packed 16-byte aligned")
+    if reference_only:
+        print(json.dumps({"impl": "reference", "metric": "weight-switch GB/s", "value": gb / (ref_ms / 1e3),
+                          "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": 1, "ms_per_step": ref_ms,
+                          "higher_is_better": True, "config": {"workload": workload},
+                          "cpu_baseline": {"value": gb / (ref_ms / 1e3), "unit": "GB/s", "cores": 1, "kind": "reference",
+                                           "sample": "the reference's per-parameter copy_ loop (torch), whole model"},
+                          "e2e": {"value": gb / (ref_ms / 1e3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    res = {"reference_loop_ms": ref_ms,
+           "dma_ms": _time_calls(lambda: ops.copy_segments(arena, cache, offs, offs, sizes, engine="dma"), reps,
+                                 device, stream),
+           "sm_ms": _time_calls(lambda: ops.copy_segments(arena, cache, offs, offs, sizes, engine="sm"), reps,
+                                device, stream)}
+    big = min(total, 1 << 30)
+    res["link_contiguous_ms"] = _time_calls(lambda: arena[:big].copy_(cache[:big], non_blocking=True), 5, device, stream)
+    ok = torch.equal(arena[: 1 << 20].cpu(), cache[: 1 << 20])
+    gbs = {k.replace("_ms", "_gbs"): (big if k.startswith("link") else total) / (v / 1e3) / 1e9 for k, v in res.items()}
+    best = max(gbs["dma_gbs"], gbs["sm_gbs"])
+    print(json.dumps({
+        "metric": "weight-switch GB/s", "value": best, "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": 1,
+        "ms_per_step": min(res["dma_ms"], res["sm_ms"]), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic parameter bytes", "config": {"workload": workload},
+        "detail_ms": res, "detail_gbs": gbs, "first_mib_matches": ok,
+        "roofline": {"bound": "host link", "achieved": best, "peak": gbs["link_contiguous_gbs"], "unit": "GB/s",
+                     "frac": best / gbs["link_contiguous_gbs"],
+                     "peak_source": "measured here: one contiguous 1 GiB pinned host-to-device copy"},
+        "cpu_baseline": {"value": gbs["reference_loop_gbs"], "unit": "GB/s", "cores": 1, "kind": "reference",
+                         "sample": "the reference's per-parameter copy_ loop (torch), whole model"},
+    }), flush=True)
+
+
 def _prep_batches():
     """(name, seq_lens, context_lens, block lists) of the step-input benchmark: the cfg2 and cfg3
     decode batches and a mixed batch of 32 prompts (lognormal lengths) with 224 decode requests."""
@@ -714,6 +799,9 @@ def run_reference(args, world, rank):
         return
     from aegaeon_b200 import synth
 
+    if args.config == "weights":
+        run_weights(args, world, rank, int(os.environ.get("LOCAL_RANK", "0")), reference_only=True)
+        return
     if args.config == "prep":
         print(json.dumps({"impl": "reference", "metric": "step-input prep us",
                           "unavailable": "the reference builds step inputs in Python inside Worker (ray, vLLM); "
@@ -783,6 +871,9 @@ def main():
         elif args.config == "prep":
             if rank == 0:
                 run_prep(args, world, rank, local)
+        elif args.config == "weights":
+            if rank == 0:
+                run_weights(args, world, rank, local)
         else:
             run_decode(args, world, rank, local)
     finally:

@@ -12,6 +12,7 @@
  *                          from the model forward at aegaeon/aegaeon/worker.py:517-523
  *   aeg_migrate_blocks     the GPU->GPU migration the reference stubs (worker.py:841-872), with
  *   aeg_ipc_export/open    the KV-cache IPC handle exchange it plans (cuda_wrapper.py:77-104)
+ *   aeg_copy_segments      the per-parameter weight-switch copies (worker.py:358-365)
  *   aeg_prepare_step_inputs the per-step Python loops of Worker._prepare_model_inputs
  *                          (worker.py:596-682), on the device
  *   aeg_decode_plan +      vLLM 0.5.1 FlashAttention backend decode call
@@ -196,6 +197,30 @@ AEG_API int aeg_prepare_step_inputs(const int32_t* block_tables, int table_strid
  * cell within a call land in an unspecified order. */
 AEG_API int aeg_update_block_tables(int32_t* block_tables, int table_stride, int rows,
                                     const int32_t* d_updates, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * f3. Model-weight switch: the prefetched model's parameters, page-locked host model cache ->
+ * device weight arena, in one call. Replaces the per-parameter loop of the reference
+ * (`new_storage.copy_(param.untyped_storage(), non_blocking=True)` for every parameter,
+ * aegaeon/aegaeon/worker.py:358-365; model cache registered at aegaeon/aegaeon/loader/loader.py:187-197;
+ * device slices from the bump allocator, aegaeon/aegaeon/allocator.py:54-81).
+ *
+ * For i < n: copies sizes[i] bytes from src_base + src_offsets[i] to dst_base + dst_offsets[i]
+ * (HOST arrays, all validated before anything is enqueued; destination segments must not
+ * overlap). engine:
+ *   AEG_COPY_ENGINE_DMA  one cudaMemcpyAsync per run of segments adjacent on both sides;
+ *                        `workspace` unused.
+ *   AEG_COPY_ENGINE_SM   one kernel for all segments through the mapped address of page-locked
+ *                        host memory (device memory as is); needs a device `workspace` of
+ *                        aeg_copy_segments_workspace_size(n) bytes, into which the segment table is
+ *                        staged with a pageable copy (that copy first waits for earlier work on
+ *                        `stream`). */
+#define AEG_COPY_ENGINE_DMA 0
+#define AEG_COPY_ENGINE_SM 1
+AEG_API size_t aeg_copy_segments_workspace_size(int64_t n);
+AEG_API int aeg_copy_segments(void* dst_base, const void* src_base, const int64_t* src_offsets,
+                              const int64_t* dst_offsets, const int64_t* sizes, int64_t n, int engine,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * a6. reshape_and_cache — replaces vLLM 0.5.1 `reshape_and_cache_flash(key, value, key_cache,

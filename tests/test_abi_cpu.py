@@ -169,3 +169,33 @@ def test_migration_ops_fail_loudly_without_cuda():
         ops.open_kv_cache(b"short", 4, 1024)
     with pytest.raises(ValueError, match="CUDA"):
         ops.export_kv_cache(kv)
+
+
+def test_segment_copy_validation_on_host():
+    lib = _native.lib
+    inval = _native.AEG_ERR_INVALID_ARGUMENT
+    p, _k = _fake()
+    o = np.array([0, 64], np.int64)
+    sz = np.array([64, 64], np.int64)
+    neg = np.array([0, -1], np.int64)
+    assert lib.aeg_copy_segments(p, p, o.ctypes.data, o.ctypes.data, sz.ctypes.data, 0, 0, None, 0, None) == 0
+    assert lib.aeg_copy_segments(p, p, o.ctypes.data, o.ctypes.data, sz.ctypes.data, -1, 0, None, 0, None) == inval
+    assert lib.aeg_copy_segments(None, p, o.ctypes.data, o.ctypes.data, sz.ctypes.data, 2, 0, None, 0, None) == inval
+    assert lib.aeg_copy_segments(p, p, o.ctypes.data, o.ctypes.data, sz.ctypes.data, 2, 7, None, 0, None) == inval
+    assert lib.aeg_copy_segments(p, p, neg.ctypes.data, o.ctypes.data, sz.ctypes.data, 2, 0, None, 0, None) == inval
+    assert lib.aeg_copy_segments(p, p, o.ctypes.data, o.ctypes.data, sz.ctypes.data, 2, 1, None, 0, None) == inval
+    assert lib.aeg_copy_segments_workspace_size(10) >= 10 * 32 and lib.aeg_copy_segments_workspace_size(0) == 0
+
+
+def test_tensor_segments_helper():
+    import torch
+
+    from aegaeon_b200 import ops
+
+    storage = torch.zeros(1000, dtype=torch.uint8)
+    a = storage[16:116].view(torch.float16)
+    b = storage[128:128 + 40]
+    offs, sizes = ops.tensor_segments([a, b], storage)
+    assert offs.tolist() == [16, 128] and sizes.tolist() == [100, 40]
+    with pytest.raises(ValueError):
+        ops.tensor_segments([torch.zeros(4)], storage)
