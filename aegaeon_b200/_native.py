@@ -50,6 +50,8 @@ SIGNATURES = {
     "aeg_ipc_close": (_i32, [_c_void_p]),
     "aeg_migrate_blocks": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "aeg_migrate_blocks_dma": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _sz, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "aeg_prefill_attention": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64,
+                                     _i32, _i32, _i32, _i32, _i32, ctypes.c_float, _i32, _c_void_p]),
     "aeg_copy_segments_workspace_size": (_sz, [_i64]),
     "aeg_copy_segments": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _c_void_p, _sz,
                                  _c_void_p]),

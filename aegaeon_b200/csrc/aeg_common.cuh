@@ -60,6 +60,7 @@ uint32_t deverr_read_and_clear_copy(cudaStream_t s, cudaError_t* err);
 uint32_t deverr_read_and_clear_cache(cudaStream_t s, cudaError_t* err);
 uint32_t deverr_read_and_clear_attn(cudaStream_t s, cudaError_t* err);
 uint32_t deverr_read_and_clear_step(cudaStream_t s, cudaError_t* err);
+uint32_t deverr_read_and_clear_prefill(cudaStream_t s, cudaError_t* err);
 
 // ---------------------------------------------------------------------------------------
 // Device helpers.

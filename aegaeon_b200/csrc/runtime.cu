@@ -47,14 +47,15 @@ const char* aeg_last_error(void) { return aeg::t_last_error.c_str(); }
 int aeg_read_device_errors(void* stream, uint32_t* flags) {
   AEG_CHECK_ARG(flags != nullptr, "aeg_read_device_errors: flags is NULL");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e1 = cudaSuccess, e2 = cudaSuccess, e3 = cudaSuccess, e4 = cudaSuccess;
-  uint32_t f = aeg::deverr_read_and_clear_copy(s, &e1);
-  f |= aeg::deverr_read_and_clear_cache(s, &e2);
-  f |= aeg::deverr_read_and_clear_attn(s, &e3);
-  f |= aeg::deverr_read_and_clear_step(s, &e4);
-  cudaError_t e = e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : (e3 != cudaSuccess ? e3 : e4));
-  if (e != cudaSuccess)
-    return aeg::set_error(AEG_ERR_CUDA, "aeg_read_device_errors: %s", cudaGetErrorString(e));
+  cudaError_t e[5] = {cudaSuccess, cudaSuccess, cudaSuccess, cudaSuccess, cudaSuccess};
+  uint32_t f = aeg::deverr_read_and_clear_copy(s, &e[0]);
+  f |= aeg::deverr_read_and_clear_cache(s, &e[1]);
+  f |= aeg::deverr_read_and_clear_attn(s, &e[2]);
+  f |= aeg::deverr_read_and_clear_step(s, &e[3]);
+  f |= aeg::deverr_read_and_clear_prefill(s, &e[4]);
+  for (cudaError_t x : e)
+    if (x != cudaSuccess)
+      return aeg::set_error(AEG_ERR_CUDA, "aeg_read_device_errors: %s", cudaGetErrorString(x));
   *flags = f;
   return AEG_OK;
 }

@@ -273,6 +273,46 @@ def migrate_blocks(source_block_ids, target_block_ids, source, target, *, engine
 
 
 # --------------------------------------------------------------------------------------------
+# Prefill attention (vLLM 0.5.1 FlashAttention backend, prompt tokens: flash_attn_varlen_func)
+
+
+def flash_attn_varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                              max_seqlen: int, softmax_scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of every prompt over itself, the call vLLM makes for prompts:
+    ``flash_attn_varlen_func(q, k, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen,
+    softmax_scale, causal=True)``.
+
+    ``q`` [T, Hq, 128], ``k``/``v`` [T, Hkv, 128] (fp16 or bf16, token-major, head dim
+    contiguous), ``cu_seqlens`` int32 [B + 1] on the device (prompt b = tokens cu[b] .. cu[b+1] - 1),
+    ``max_seqlen`` the longest prompt. Returns ``out`` [T, Hq, 128].
+    """
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _require_cuda(t, name)
+        if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.size(2):
+            raise ValueError(f"{name} must be [tokens, heads, head_dim] with contiguous heads")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share an fp16 or bf16 dtype")
+    T, Hq, D = q.shape
+    if k.shape[0] != T or v.shape != k.shape:
+        raise ValueError("k and v must be [tokens, Hkv, head_dim] with q's token count")
+    _require_cuda(cu_seqlens, "cu_seqlens")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or not cu_seqlens.is_contiguous():
+        raise ValueError("cu_seqlens must be a contiguous int32 vector")
+    if out is None:
+        out = torch.empty_like(q)
+    if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or out.stride(1) != D:
+        raise ValueError("out must match q")
+    dev = q.device
+    with torch.cuda.device(dev):
+        st = lib.aeg_prefill_attention(out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(),
+                                       k.stride(0), v.data_ptr(), v.stride(0), cu_seqlens.data_ptr(), T,
+                                       cu_seqlens.numel() - 1, int(max_seqlen), Hq, k.size(1), D, float(softmax_scale),
+                                       _DTYPES[q.dtype], _stream(dev))
+    check(st, "prefill_attention")
+    return out
+
+
+# --------------------------------------------------------------------------------------------
 # Model-weight switch (aegaeon/aegaeon/worker.py:358-365: one copy_ per parameter)
 
 

@@ -42,7 +42,7 @@ def _args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate", "prep", "weights"])
+    p.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "migrate", "prep", "weights", "prefill"])
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--unfused", action="store_true",
@@ -707,6 +707,96 @@ def run_weights(args, world, rank, local, reference_only=False):
     }), flush=True)
 
 
+def _prefill_lengths(scale: float = 1.0):
+    """Prompt lengths of the prefill workload: 16 prompts, round(lognormal(6.5, 0.8)) clipped to
+    [16, 8192], seed 7 (Qwen2.5-7B heads: 28 query, 4 KV, head dim 128)."""
+    rng = np.random.default_rng(7)
+    n = max(1, int(round(16 * scale)))
+    return np.clip(np.round(rng.lognormal(6.5, 0.8, n)), 16, 8192).astype(np.int64)
+
+
+def _vllm_varlen():
+    """vLLM's bundled FlashAttention varlen kernel (the reference's kernel family), if it loads."""
+    try:
+        from vllm.vllm_flash_attn import flash_attn_varlen_func
+        return flash_attn_varlen_func, "vllm.vllm_flash_attn.flash_attn_varlen_func"
+    except Exception as e:  # noqa: BLE001 - any import failure means "not available"
+        return None, f"unavailable: {type(e).__name__}: {str(e)[:160]}"
+
+
+def run_prefill(args, world, rank, local):
+    """Prefill attention (TFLOP/s, causal FLOPs 2 x 2 x Hq x D x L(L+1)/2 per prompt): this
+    library's kernel on a batch of prompts with inputs resident, beside vLLM's FlashAttention
+    varlen kernel on the same inputs when it loads, and the oracle on one prompt of the batch."""
+    from aegaeon_b200 import ops
+    from oracle import oracle as orc
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    lens = _prefill_lengths(args.scale)
+    Hq, Hkv, D = 28, 4, 128
+    T = int(lens.sum())
+    flops = float(sum(4.0 * Hq * D * L * (L + 1) / 2 for L in lens))
+    cu = torch.as_tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=device)
+    scale = D ** -0.5
+    peak, peak_src = _peaks()
+    peak_tf = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak_tf = float(json.load(f)["bf16_tflops"])
+    except Exception:  # noqa: BLE001
+        peak_tf = 1590.0
+    res = {}
+    fa, fa_note = _vllm_varlen()
+    for dtype in (torch.bfloat16, torch.float16):
+        g = torch.Generator(device=device).manual_seed(11)
+        q = torch.randn((T, Hq, D), generator=g, device=device).to(dtype)
+        k = torch.randn((T, Hkv, D), generator=g, device=device).to(dtype)
+        v = torch.randn((T, Hkv, D), generator=g, device=device).to(dtype)
+        out = torch.empty_like(q)
+        reps = max(3, min(args.steps, 20))
+        ms = _time_calls(lambda: ops.flash_attn_varlen_prefill(q, k, v, cu, int(lens.max()), scale, out=out), reps,
+                         device, stream)
+        name = "bf16" if dtype == torch.bfloat16 else "fp16"
+        res[name] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12}
+        if fa is not None:
+            try:
+                call = lambda: fa(q, k, v, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=int(lens.max()),  # noqa: E731
+                                  max_seqlen_k=int(lens.max()), softmax_scale=scale, causal=True)
+                fa_ms = _time_calls(call, reps, device, stream)
+                ref_out = call()
+                torch.cuda.synchronize(device)
+                res[name]["vllm_fa_ms"] = fa_ms
+                res[name]["vllm_fa_tflops"] = flops / (fa_ms / 1e3) / 1e12
+                res[name]["max_abs_diff_vs_vllm_fa"] = float((ref_out.float() - out.float()).abs().max())
+            except Exception as e:  # noqa: BLE001
+                res[name]["vllm_fa"] = f"failed: {type(e).__name__}: {str(e)[:160]}"
+    # CPU baseline: the oracle (numpy, fp64) on the batch's shortest prompt of at least 256 tokens
+    Ls = int(min([L for L in lens if L >= 256] or [int(lens.min())]))
+    rng = np.random.default_rng(0)
+    qb, kb, vb = (orc.f64_to_bits(rng.standard_normal((Ls, h, D)), orc.BF16) for h in (Hq, Hkv, Hkv))
+    t0 = time.perf_counter()
+    orc.np_prefill_attention(qb, kb, vb, [0, Ls], scale, orc.BF16)
+    cpu_s = time.perf_counter() - t0
+    cpu_tf = 4.0 * Hq * D * Ls * (Ls + 1) / 2 / cpu_s / 1e12
+    b = res["bf16"]
+    print(json.dumps({
+        "metric": "prefill-attn TFLOP/s", "value": b["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": reps,
+        "warmup": 1, "ms_per_step": b["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic N(0,1) q/k/v",
+        "config": {"workload": f"{len(lens)} prompts, lengths round(lognormal(6.5, 0.8)) in [16, 8192] (sum {T}, "
+                               f"max {int(lens.max())}), causal, Hq 28 / Hkv 4 / D 128",
+                   "prompt_lengths": lens.tolist()},
+        "detail": res, "vllm_fa": fa_note,
+        "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel (mma.sync m16n8k16)", "achieved": b["tflops"],
+                     "peak": peak_tf, "unit": "TFLOP/s", "frac": b["tflops"] / peak_tf,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"},
+        "cpu_baseline": {"value": cpu_tf, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                         "sample": f"the oracle (numpy fp64) on one {Ls}-token prompt, all 28 heads"},
+    }), flush=True)
+
+
 def _prep_batches():
     """(name, seq_lens, context_lens, block lists) of the step-input benchmark: the cfg2 and cfg3
     decode batches and a mixed batch of 32 prompts (lognormal lengths) with 224 decode requests."""
@@ -802,6 +892,12 @@ def run_reference(args, world, rank):
     if args.config == "weights":
         run_weights(args, world, rank, int(os.environ.get("LOCAL_RANK", "0")), reference_only=True)
         return
+    if args.config == "prefill":
+        print(json.dumps({"impl": "reference", "metric": "prefill-attn TFLOP/s",
+                          "unavailable": "the reference's prefill attention is vLLM 0.5.1's FlashAttention (absent); "
+                                         "--config prefill times vLLM's bundled FlashAttention beside this library"}),
+              flush=True)
+        return
     if args.config == "prep":
         print(json.dumps({"impl": "reference", "metric": "step-input prep us",
                           "unavailable": "the reference builds step inputs in Python inside Worker (ray, vLLM); "
@@ -874,6 +970,9 @@ def main():
         elif args.config == "weights":
             if rank == 0:
                 run_weights(args, world, rank, local)
+        elif args.config == "prefill":
+            if rank == 0:
+                run_prefill(args, world, rank, local)
         else:
             run_decode(args, world, rank, local)
     finally:

@@ -13,6 +13,7 @@
  *   aeg_migrate_blocks     the GPU->GPU migration the reference stubs (worker.py:841-872), with
  *   aeg_ipc_export/open    the KV-cache IPC handle exchange it plans (cuda_wrapper.py:77-104)
  *   aeg_copy_segments      the per-parameter weight-switch copies (worker.py:358-365)
+ *   aeg_prefill_attention  vLLM 0.5.1 FlashAttention backend prompt call `flash_attn_varlen_func`
  *   aeg_prepare_step_inputs the per-step Python loops of Worker._prepare_model_inputs
  *                          (worker.py:596-682), on the device
  *   aeg_decode_plan +      vLLM 0.5.1 FlashAttention backend decode call
@@ -221,6 +222,26 @@ AEG_API size_t aeg_copy_segments_workspace_size(int64_t n);
 AEG_API int aeg_copy_segments(void* dst_base, const void* src_base, const int64_t* src_offsets,
                               const int64_t* dst_offsets, const int64_t* sizes, int64_t n, int engine,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * f2. Prefill (prompt) attention. Replaces vLLM 0.5.1's FlashAttention backend call for prompts,
+ * `flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+ * softmax_scale, causal=True)` with q and k lengths equal (Aegaeon prefills whole prompts without
+ * chunking, aegaeon/aegaeon/worker.py:603-626; the prompt's K/V also go to the paged cache
+ * through aeg_reshape_and_cache).
+ *
+ * q [num_tokens, Hq, D], k/v [num_tokens, Hkv, D], out [num_tokens, Hq, D] (token strides in
+ * elements; q/k/v 16-byte aligned with strides that are multiples of 8), prompt b = tokens
+ * cu_seqlens[b] .. cu_seqlens[b + 1] - 1 (DEVICE int32 [B + 1]); max_seqlen >= every prompt's
+ * length. For query token i of a prompt:
+ *   out[i, h] = softmax_j(scale * q[i, h] . k[j, h / (Hq / Hkv)]) . v[j, h / (Hq / Hkv)], j = 0 .. i
+ * fp32 accumulation, output rounded to the input dtype. D = 128. A prompt whose range leaves
+ * [0, num_tokens) or exceeds max_seqlen is skipped (its rows are not written) and raises
+ * AEG_DEVERR_SEQ_LEN_RANGE. */
+AEG_API int aeg_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                  const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                                  const int32_t* cu_seqlens, int64_t num_tokens, int B, int max_seqlen,
+                                  int Hq, int Hkv, int D, float scale, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * a6. reshape_and_cache — replaces vLLM 0.5.1 `reshape_and_cache_flash(key, value, key_cache,

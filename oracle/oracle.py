@@ -22,6 +22,7 @@ Reference anchors (paths inside the reference checkout):
                      worker.py:640-653; layout worker.py:388-451, config.py:256-271
   slot mapping       aegaeon/aegaeon/worker.py:596-682; padding aegaeon/aegaeon/utils.py:241-257
   step inputs        the same function: positions, offsets, decode/prompt table rows (np_step_inputs)
+  prefill attention  vLLM 0.5.1 prompt call flash_attn_varlen_func(..., causal=True) (np_prefill_attention)
 
 Parity pins: the reference ships no kernel tests or golden vectors (its tests are smoke scripts
 without numeric assertions). ``swap`` is pinned against the reference's own operator compiled
@@ -193,6 +194,33 @@ def np_slot_mapping(seq_lens, context_lens, tables) -> np.ndarray:
         for i in range(c, n):
             slots.append(int(t[i // 16]) * 16 + i % 16)
     return np.asarray(slots, dtype=np.int64)
+
+
+def np_prefill_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seqlens, scale: float,
+                         dtype: int) -> np.ndarray:
+    """Causal prompt attention, restated from vLLM 0.5.1's prompt call
+    ``flash_attn_varlen_func(q, k, v, cu, cu, max_len, max_len, softmax_scale, causal=True)``
+    (Aegaeon prefills whole prompts, aegaeon/aegaeon/worker.py:603-626): query i of prompt b sees
+    keys 0..i of the same prompt, query head h reads KV head h // (Hq // Hkv); double precision,
+    output rounded to ``dtype``. q/k/v are 16-bit patterns [T, H, D]."""
+    qf, kf, vf = (bits_to_f64(x, dtype) for x in (q, k, v))
+    T, Hq, D = qf.shape
+    G = Hq // kf.shape[1]
+    out = np.zeros((T, Hq, D))
+    for b in range(len(cu_seqlens) - 1):
+        s0, s1 = int(cu_seqlens[b]), int(cu_seqlens[b + 1])
+        L = s1 - s0
+        if L <= 0:
+            continue
+        mask = np.triu(np.ones((L, L), dtype=bool), 1)
+        for h in range(Hq):
+            S = qf[s0:s1, h] @ kf[s0:s1, h // G].T * scale
+            S[mask] = -np.inf
+            S -= S.max(axis=1, keepdims=True)
+            P = np.exp(S)
+            P /= P.sum(axis=1, keepdims=True)
+            out[s0:s1, h] = P @ vf[s0:s1, h // G]
+    return f64_to_bits(out, dtype)
 
 
 def np_step_inputs(seq_lens, context_lens, tables) -> dict:

@@ -1,0 +1,101 @@
+"""Prefill (prompt) attention on the GPU (``ops.flash_attn_varlen_prefill``): against the fp64
+oracle (atol 2e-3 / rtol 1e-2, the attention tolerance of this path) on small varlen batches, and
+against torch fp32 scaled-dot-product attention per prompt on larger ones. Also the prompt half
+of the cache write: reshape_and_cache over a batch of prompts' tokens, bit-exact."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from aegaeon_b200 import ops
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DT = {torch.float16: orc.FP16, torch.bfloat16: orc.BF16}
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _inputs(dev, lens, Hq, Hkv, dtype, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    T = int(sum(lens))
+    q = torch.randn((T, Hq, 128), generator=g, device=dev).to(dtype)
+    k = torch.randn((T, Hkv, 128), generator=g, device=dev).to(dtype)
+    v = torch.randn((T, Hkv, 128), generator=g, device=dev).to(dtype)
+    cu = torch.as_tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=dev)
+    return q, k, v, cu
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (8, 8)])
+def test_prefill_matches_oracle(cuda_device, dtype, Hq, Hkv):
+    lens = [1, 17, 64, 65, 0, 130]
+    q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 3)
+    scale = 128 ** -0.5
+    out = ops.flash_attn_varlen_prefill(q, k, v, cu, max(lens), scale)
+    torch.cuda.synchronize()
+    want = orc.np_prefill_attention(_bits(q), _bits(k), _bits(v), cu.cpu().numpy(), scale, DT[dtype])
+    ok, err, excess = orc.compare_attention(_bits(out), want, DT[dtype])
+    assert ok, (err, excess)
+    assert ops.read_device_errors(cuda_device) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_long_prompts_match_torch_fp32(cuda_device, dtype):
+    lens = [2048, 777, 1, 1500]
+    Hq, Hkv = 28, 4
+    q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 5)
+    scale = 128 ** -0.5
+    out = ops.flash_attn_varlen_prefill(q, k, v, cu, max(lens), scale)
+    torch.cuda.synchronize()
+    c = cu.cpu().tolist()
+    for b in range(len(lens)):
+        s0, s1 = c[b], c[b + 1]
+        qq = q[s0:s1].float().transpose(0, 1)                                      # [Hq, L, D]
+        kk = k[s0:s1].float().transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)
+        vv = v[s0:s1].float().transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)
+        ref = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=scale).transpose(0, 1)
+        got = out[s0:s1].float()
+        tol = 2e-3 + 1e-2 * ref.abs()
+        assert bool(((got - ref).abs() <= tol).all()), (b, float((got - ref).abs().max()))
+
+
+def test_prefill_rejects_out_of_range_prompts(cuda_device):
+    lens = [10, 20]
+    q, k, v, cu = _inputs(cuda_device, lens, 8, 8, torch.float16, 1)
+    out = torch.zeros_like(q)
+    bad = torch.as_tensor([0, 10, 40], dtype=torch.int32, device=cuda_device)  # prompt 1 runs past the 30 tokens
+    ops.flash_attn_varlen_prefill(q, k, v, bad, 30, 128 ** -0.5, out=out)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) & 0x4
+    assert not out[10:].any()  # the bad prompt's rows were not written
+    ref = ops.flash_attn_varlen_prefill(q, k, v, cu, 20, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.equal(out[:10], ref[:10])
+
+
+def test_prompt_cache_write_bit_exact(cuda_device):
+    """reshape_and_cache of a batch of prompts (slots from the step-input restatement)."""
+    rng = np.random.default_rng(9)
+    lens = [300, 45, 1, 1024]
+    N, L, Hkv = 128, 2, 4
+    perm = rng.permutation(N)
+    tables, off = [], 0
+    for n in lens:
+        nb = (n + 15) // 16
+        tables.append(perm[off:off + nb].tolist())
+        off += nb
+    slots = orc.np_step_inputs(lens, [0] * len(lens), tables)["slot_mapping"]
+    T = len(slots)
+    kv = torch.randint(-32768, 32768, (N, L, 2, 16, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    key = torch.randint(-32768, 32768, (T, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    val = torch.randint(-32768, 32768, (T, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    kv_dev = kv.to(cuda_device).view(torch.bfloat16)
+    ops.reshape_and_cache(key.to(cuda_device).view(torch.bfloat16), val.to(cuda_device).view(torch.bfloat16), kv_dev,
+                          1, torch.as_tensor(slots, device=cuda_device))
+    ref = kv.numpy().view(np.uint16).copy()
+    orc.np_reshape_and_cache(key.numpy().view(np.uint16), val.numpy().view(np.uint16), ref[:, 1, 0], ref[:, 1, 1], slots)
+    assert np.array_equal(_bits(kv_dev), ref)
