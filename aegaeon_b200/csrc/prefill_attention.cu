@@ -16,6 +16,9 @@
 // of a prompt sees the most keys).
 #include "aeg_common.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 #include <type_traits>
 
@@ -270,6 +273,471 @@ int launch_prefill(void* out, int64_t o_stride, const void* q, int64_t q_stride,
   return AEG_OK;
 }
 
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 kernel. One CTA = 256 query rows of one head of one prompt as two 128-row tiles A and
+// B, each owned by a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row
+// t of its tile = TMEM lane t), plus an issuer warp (warp 8) whose first thread issues every TMA
+// load and every tcgen05.mma. Keys come in tiles of 64 through a 3-stage TMA ring shared by both
+// query tiles. Per key tile j and query tile X:
+//   S_X(j) = Q_X K(j)^T  8 MMAs (M 128, N 64, K 16) into TMEM S_X[j & 1] (64 columns);
+//   softmax               the warpgroup reads its rows of S_X(j) (tcgen05.ld, two passes: max,
+//                         then exp2 / sum / P), writes P in the input dtype to an SW128 K-major
+//                         shared tile (bf16: plus its rounding residue to a second tile);
+//   O_X += P V(j)          4 MMAs (M 128, N 128, K 16) into TMEM O_X, V read MN-major straight from
+//                         its TMA layout.
+// O never leaves TMEM until the end: a row is rescaled in place (tcgen05.ld / st) only when its
+// running maximum grows by more than 8 in the exp2 domain, so P stays below 2^8. While one
+// warpgroup runs its softmax the tensor pipe works on the other tile's MMAs. Every wait is
+// bounded: a timeout is recorded, the CTA stops issuing, drains its own loads (bounded), frees
+// TMEM and returns without writing.
+constexpr int kTM = 128;                 // query rows per tile (two tiles per CTA)
+constexpr int kTN = 64;                  // keys per tile
+constexpr int kTStages = 3;
+constexpr int kTThreads = 9 * 32;        // 2 softmax warpgroups + the issuer warp
+constexpr int kQHalf = kTM * 128;        // one SW128 box of Q: 128 rows x 64 elements (16 KiB)
+constexpr int kKHalf = kTN * 128;        // one SW128 box of K or V: 64 rows x 64 elements (8 KiB)
+constexpr int kOffQ = 0;                                  // Q_A, Q_B: 2 halves each
+constexpr int kOffK = kOffQ + 4 * kQHalf;                 // stage s: 2 halves
+constexpr int kOffV = kOffK + kTStages * 2 * kKHalf;      // stage s: 2 halves
+constexpr int kOffP = kOffV + kTStages * 2 * kKHalf;      // P_A, P_B: 128 rows x 64 keys
+constexpr int kOffPl = kOffP + 2 * kQHalf;                // bf16 residues of P_A, P_B
+constexpr int kOffBar = kOffPl + 2 * kQHalf;
+constexpr int kTSmem = kOffBar + 256 + 1024;              // + 1024-byte alignment slack
+constexpr uint32_t kTmemCols = 512;                       // S_A[2], S_B[2] (64 each), O_A, O_B (128 each)
+constexpr uint64_t kTcWaitNs = 2000000000ull;
+constexpr float kRescaleAbove = 8.f;                      // exp2 domain
+
+// mbarrier slots
+constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = 4, kBarKFree = 7, kBarVFree = 10, kBarSFull = 13,  // S: [X][buf]
+    kBarPFull = 17, kBarPv = 19, kBarDrain = 21, kBarCount = 22;
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// SW128 smem matrix descriptor (version 1): start >> 4, LBO >> 4, SBO >> 4, layout type 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16, fp32 accumulator, M = 128, A K-major.
+template <typename T>
+__device__ __forceinline__ uint32_t idesc_f16(int n, bool b_mn_major) {
+  const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((static_cast<uint32_t>(n) >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// OR of `v` over the 128 threads of named barrier `id` (a barrier itself: every thread must come).
+__device__ __forceinline__ bool group_any(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, 128, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTThreads, 1)
+prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t o_stride,
+                  const int32_t* __restrict__ cu_seqlens, int64_t num_tokens, int max_seqlen, int G,
+                  float scale_log2) {
+  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t tsmem_raw[];
+  const uint32_t raw = smem_u32(tsmem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = tsmem_raw + (base - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8 * kBarCount);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kOffBar + 8 * kBarCount + 4);  // the issuer gave up
+  auto bar_u32 = [&](int i) { return base + kOffBar + 8u * static_cast<uint32_t>(i); };
+
+  const int tile_m = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // heaviest first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int s0 = cu_seqlens[b];
+  const int L = cu_seqlens[b + 1] - s0;
+  if (s0 < 0 || L < 0 || static_cast<int64_t>(s0) + L > num_tokens || L > max_seqlen) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && h == 0) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
+    return;
+  }
+  const int q0 = tile_m * 2 * kTM;
+  if (L == 0 || q0 >= L) return;
+  const int kvh = h / G;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const bool has_b = q0 + kTM < L;
+  const int nA = (min(L, q0 + kTM) + kTN - 1) / kTN;                  // key tiles tile A needs
+  const int nB = has_b ? (min(L, q0 + 2 * kTM) + kTN - 1) / kTN : 0;  // and tile B
+  const int n_tiles = has_b ? nB : nA;
+
+  if (tid == 0) {
+    for (int i = 0; i < kBarCount; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    *s_abort = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto tmem_s = [&](int x, int buf) { return tmem + static_cast<uint32_t>((x * 2 + buf) * 64); };
+  auto tmem_o = [&](int x) { return tmem + 256u + static_cast<uint32_t>(x) * 128u; };
+  const uint32_t sQ = base + kOffQ;
+  auto sQx = [&](int x) { return sQ + static_cast<uint32_t>(x) * 2 * kQHalf; };
+  auto sK = [&](int st) { return base + kOffK + static_cast<uint32_t>(st) * 2 * kKHalf; };
+  auto sV = [&](int st) { return base + kOffV + static_cast<uint32_t>(st) * 2 * kKHalf; };
+  auto sP = [&](int x) { return base + kOffP + static_cast<uint32_t>(x) * kQHalf; };
+  auto sPl = [&](int x) { return base + kOffPl + static_cast<uint32_t>(x) * kQHalf; };
+
+  bool abort = false;
+  if (warp == 8) {
+    // ------------------------------- issuer -------------------------------
+    if ((tid & 31) == 0) {
+      auto issue_kv = [&](int t) {
+        const int st = t % kTStages;
+        const int y = s0 + t * kTN, x = kvh * 128;
+        mbar_arrive_expect_tx(&bars[kBarKFull + st], 2 * kKHalf);
+        tma_load_2d(sK(st), &kmap, bar_u32(kBarKFull + st), x, y);
+        tma_load_2d(sK(st) + kKHalf, &kmap, bar_u32(kBarKFull + st), x + 64, y);
+        mbar_arrive_expect_tx(&bars[kBarVFull + st], 2 * kKHalf);
+        tma_load_2d(sV(st), &vmap, bar_u32(kBarVFull + st), x, y);
+        tma_load_2d(sV(st) + kKHalf, &vmap, bar_u32(kBarVFull + st), x + 64, y);
+      };
+      mbar_arrive_expect_tx(&bars[kBarQ], (has_b ? 4 : 2) * kQHalf);
+      tma_load_2d(sQx(0), &qmap, bar_u32(kBarQ), h * 128, s0 + q0);
+      tma_load_2d(sQx(0) + kQHalf, &qmap, bar_u32(kBarQ), h * 128 + 64, s0 + q0);
+      if (has_b) {
+        tma_load_2d(sQx(1), &qmap, bar_u32(kBarQ), h * 128, s0 + q0 + kTM);
+        tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQ), h * 128 + 64, s0 + q0 + kTM);
+      }
+      int issued = 0;
+      for (; issued < min(kTStages, n_tiles); ++issued) issue_kv(issued);
+      const uint32_t id_s = idesc_f16<T>(kTN, false), id_o = idesc_f16<T>(128, true);
+      bool ok = mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs);
+      int done_k = 0;  // key tiles whose K and V loads were seen landing
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kTStages;
+        const uint32_t ph = static_cast<uint32_t>((j / kTStages) & 1);
+        ok = mbar_wait_bounded(&bars[kBarKFull + st], ph, kTcWaitNs);
+        if (!ok) break;
+        tc_fence_after();
+        for (int x = 0; x < 2; ++x) {
+          if (j >= (x == 0 ? nA : nB)) continue;
+          // S_x[j & 1] last held S_x(j - 2), which softmax x finished reading before it published
+          // P_x(j - 2); this thread waited for that before issuing O_x += P_x V(j - 2).
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t qo = static_cast<uint32_t>(kk >> 2) * kQHalf + static_cast<uint32_t>(kk & 3) * 32;
+            const uint32_t ko = static_cast<uint32_t>(kk >> 2) * kKHalf + static_cast<uint32_t>(kk & 3) * 32;
+            umma_f16(tmem_s(x, j & 1), sw128_desc(sQx(x) + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
+                     kk > 0);
+          }
+          umma_commit(bar_u32(kBarSFull + x * 2 + (j & 1)));
+        }
+        if (!ok) break;
+        umma_commit(bar_u32(kBarKFree + st));
+        // refill the stage of tile j - 1 (its MMAs precede S(j) in the tensor pipe) with tile j + 2
+        if (j >= 1 && issued < n_tiles) {
+          const int ps = (j - 1) % kTStages;
+          const uint32_t pph = static_cast<uint32_t>(((j - 1) / kTStages) & 1);
+          ok = mbar_wait_bounded(&bars[kBarKFree + ps], pph, kTcWaitNs) &&
+               mbar_wait_bounded(&bars[kBarVFree + ps], pph, kTcWaitNs);
+          if (!ok) break;
+          issue_kv(issued++);
+        }
+        ok = mbar_wait_bounded(&bars[kBarVFull + st], ph, kTcWaitNs);
+        if (!ok) break;
+        done_k = j + 1;
+        for (int x = 0; x < 2; ++x) {
+          if (j >= (x == 0 ? nA : nB)) continue;
+          ok = mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_f16(tmem_o(x), sw128_desc(sP(x) + kk * 32, 16, 1024), sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kSplitP)
+              umma_f16(tmem_o(x), sw128_desc(sPl(x) + kk * 32, 16, 1024), sw128_desc(sV(st) + kk * 2048, kKHalf, 1024),
+                       id_o, 1u);
+          }
+          umma_commit(bar_u32(kBarPv + x));
+        }
+        if (!ok) break;
+        umma_commit(bar_u32(kBarVFree + st));
+      }
+      if (ok && n_tiles > 0) {  // the last tile's release commits have landed before the CTA exits
+        const int t = n_tiles - 1;
+        const uint32_t tph = static_cast<uint32_t>((t / kTStages) & 1);
+        ok = mbar_wait_bounded(&bars[kBarKFree + t % kTStages], tph, kTcWaitNs) &&
+             mbar_wait_bounded(&bars[kBarVFree + t % kTStages], tph, kTcWaitNs);
+      }
+      // every MMA this thread issued has completed before TMEM is freed
+      umma_commit(bar_u32(kBarDrain));
+      if (!mbar_wait_bounded(&bars[kBarDrain], 0, kTcWaitNs)) ok = false;
+      if (!ok) {
+        *s_abort = 1;
+        __threadfence_block();
+        atomicOr(&g_deverr_prefill, AEG_DEVERR_WAIT_TIMEOUT);
+        // loads issued but not seen landing: wait (bounded) before the CTA can exit
+        for (int t = done_k; t < issued; ++t) {
+          const uint32_t tph = static_cast<uint32_t>((t / kTStages) & 1);
+          mbar_wait_bounded(&bars[kBarKFull + t % kTStages], tph, kTcWaitNs);
+          mbar_wait_bounded(&bars[kBarVFull + t % kTStages], tph, kTcWaitNs);
+        }
+        // release the softmax warpgroups from any wait on this thread
+        for (int i = kBarSFull; i < kBarDrain; ++i) mbar_arrive(&bars[i]);
+      }
+      abort = !ok;
+    }
+  } else {
+    // ------------------------------- softmax warpgroup x -------------------------------
+    const int x = warp >> 2;
+    const int r = tid & 127;  // row of the tile, TMEM lane
+    const int row = q0 + x * kTM + r;
+    const int nx = x == 0 ? nA : nB;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    // tcgen05.ld / st are warp-collective (.sync.aligned): every lane of a warp executes each of them,
+    // and each wait's outcome is made uniform over the warpgroup before anyone acts on it.
+    for (int j = 0; j < nx; ++j) {
+      bool bad = !mbar_wait_bounded(&bars[kBarSFull + x * 2 + (j & 1)], static_cast<uint32_t>((j >> 1) & 1), kTcWaitNs) ||
+                 *s_abort;
+      if (group_any(1 + x, bad)) {
+        abort = true;
+        break;
+      }
+      tc_fence_after();
+      const int key0 = j * kTN;
+      const uint32_t ts = tmem_s(x, j & 1) + lane_off;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[16];
+        tmem_ld16(ts + c * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int key = key0 + c * 16 + i;
+          mx = fmaxf(mx, (key <= row && key < L) ? v[i] * scale_log2 : -INFINITY);
+        }
+      }
+      // P_x is free once O_x += P_x V(j - 1) has completed; O_x may be rescaled from then on
+      if (j > 0) {
+        bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
+        if (group_any(1 + x, bad)) {
+          abort = true;
+          break;
+        }
+      }
+      tc_fence_after();
+      const bool grow = mx > m_used + kRescaleAbove;
+      const float factor = grow ? ex2p(m_used - mx) : 1.f;  // 0 while the row has seen nothing
+      // O rows are rescaled in TMEM by the whole warp when any of its rows needs it
+      if (j > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
+        const uint32_t to = tmem_o(x) + lane_off;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float v[16];
+          tmem_ld16(to + c * 16, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] *= factor;
+          tmem_st16(to + c * 16, v);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      }
+      if (grow) {
+        l *= factor;
+        m_used = mx;
+      }
+      const float base_m = m_used == -INFINITY ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[16];
+        tmem_ld16(ts + c * 16, v);
+        uint32_t pk[8], pr[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const int key = key0 + c * 16 + i;
+          const float p0 = (key <= row && key < L) ? ex2p(v[i] * scale_log2 - base_m) : 0.f;
+          const float p1 = (key + 1 <= row && key + 1 < L) ? ex2p(v[i + 1] * scale_log2 - base_m) : 0.f;
+          rs += p0 + p1;
+          pk[i >> 1] = pack2<T>(p0, p1);
+          if constexpr (kSplitP) {
+            const float2 rr = unpack2<T>(pk[i >> 1]);
+            pr[i >> 1] = pack2<T>(p0 - rr.x, p1 - rr.y);
+          }
+        }
+        // keys c*16 .. c*16+15 of row r: 16-byte chunks 2c and 2c + 1 of the row, swizzled
+        const uint32_t roff = static_cast<uint32_t>(r) * 128;
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const uint32_t chunk = (static_cast<uint32_t>(c * 2 + q2) ^ static_cast<uint32_t>(r & 7)) * 16;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP(x) + roff + chunk), "r"(pk[4 * q2]),
+                       "r"(pk[4 * q2 + 1]), "r"(pk[4 * q2 + 2]), "r"(pk[4 * q2 + 3])
+                       : "memory");
+          if constexpr (kSplitP)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sPl(x) + roff + chunk), "r"(pr[4 * q2]),
+                         "r"(pr[4 * q2 + 1]), "r"(pr[4 * q2 + 2]), "r"(pr[4 * q2 + 3])
+                         : "memory");
+        }
+      }
+      l += rs;
+      fence_async_smem();
+      tc_fence_before();
+      group_sync(1 + x);
+      if (r == 0) mbar_arrive(&bars[kBarPFull + x]);
+    }
+    if (!abort && nx > 0) {
+      const bool bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((nx - 1) & 1), kTcWaitNs) || *s_abort;
+      abort = group_any(1 + x, bad);
+    }
+    tc_fence_after();
+    if (!abort && nx > 0) {  // warpgroup-uniform: the TMEM reads are collective, the stores per row
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* dst = out + static_cast<int64_t>(s0 + min(row, L - 1)) * o_stride + static_cast<int64_t>(h) * 128;
+      const uint32_t to = tmem_o(x) + lane_off;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(to + c * 16, v);
+        uint4 w0, w1;
+        w0.x = pack2<T>(v[0] * inv, v[1] * inv);
+        w0.y = pack2<T>(v[2] * inv, v[3] * inv);
+        w0.z = pack2<T>(v[4] * inv, v[5] * inv);
+        w0.w = pack2<T>(v[6] * inv, v[7] * inv);
+        w1.x = pack2<T>(v[8] * inv, v[9] * inv);
+        w1.y = pack2<T>(v[10] * inv, v[11] * inv);
+        w1.z = pack2<T>(v[12] * inv, v[13] * inv);
+        w1.w = pack2<T>(v[14] * inv, v[15] * inv);
+        if (row < L) {
+          *reinterpret_cast<uint4*>(dst + c * 16) = w0;
+          *reinterpret_cast<uint4*>(dst + c * 16 + 8) = w1;
+        }
+      }
+    }
+  }
+  if (abort) atomicOr(&g_deverr_prefill, AEG_DEVERR_WAIT_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D map over [rows, cols] (row stride in elements), boxes of 64 elements x box_rows, 128-byte swizzle.
+int encode_rows_map(CUtensorMap* map, const void* base, int dtype, int64_t rows, int64_t cols, int64_t row_stride,
+                    int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(AEG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype == AEG_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(AEG_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  return AEG_OK;
+}
+
+template <typename T>
+int launch_prefill_tc(void* out, int64_t o_stride, const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                      const void* v, int64_t v_stride, const int32_t* cu, int64_t num_tokens, int B, int max_seqlen,
+                      int Hq, int Hkv, float scale, int dtype, cudaStream_t stream) {
+  CUtensorMap qm, km, vm;
+  int st = encode_rows_map(&qm, q, dtype, num_tokens, int64_t(Hq) * kPD, q_stride, kTM);
+  if (st == AEG_OK) st = encode_rows_map(&km, k, dtype, num_tokens, int64_t(Hkv) * kPD, k_stride, kTN);
+  if (st == AEG_OK) st = encode_rows_map(&vm, v, dtype, num_tokens, int64_t(Hkv) * kPD, v_stride, kTN);
+  if (st != AEG_OK) return st;
+  constexpr int kMaxDevices = 64;
+  static bool configured[kMaxDevices] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  AEG_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(AEG_ERR_UNSUPPORTED, "prefill_attention: device %d", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      AEG_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmem));
+      configured[dev] = true;
+    }
+  }
+  const dim3 grid(static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)), static_cast<unsigned>(Hq),
+                  static_cast<unsigned>(B));
+  prefill_tc_kernel<T><<<grid, kTThreads, kTSmem, stream>>>(
+      qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, max_seqlen, Hq / Hkv,
+      static_cast<float>(static_cast<double>(scale) * 1.4426950408889634));
+  AEG_CHECK_LAUNCH("prefill_attention(tcgen05)");
+  return AEG_OK;
+}
+
+constexpr bool kPrefillTcgen05 = true;  // tcgen05 kernel; false selects the mma.sync kernel
 }  // namespace
 
 uint32_t deverr_read_and_clear_prefill(cudaStream_t s, cudaError_t* err) {
@@ -303,6 +771,15 @@ int aeg_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t 
                 "prefill_attention: q/k/v must be 16-byte aligned with token strides that are multiples of 8 elements");
   AEG_CHECK_ARG(max_seqlen <= (1 << 24) && B <= 65535 && Hq <= 65535, "prefill_attention: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (aeg::kPrefillTcgen05) {
+    AEG_CHECK_ARG(aeg::aligned(out, 16) && out_stride % 8 == 0,
+                  "prefill_attention: out must be 16-byte aligned with a token stride that is a multiple of 8");
+    if (dtype == AEG_DTYPE_BF16)
+      return aeg::launch_prefill_tc<__nv_bfloat16>(out, out_stride, q, q_stride, k, k_stride, v, v_stride, cu_seqlens,
+                                                   num_tokens, B, max_seqlen, Hq, Hkv, scale, dtype, s);
+    return aeg::launch_prefill_tc<__half>(out, out_stride, q, q_stride, k, k_stride, v, v_stride, cu_seqlens, num_tokens,
+                                          B, max_seqlen, Hq, Hkv, scale, dtype, s);
+  }
   if (dtype == AEG_DTYPE_BF16)
     return aeg::launch_prefill<__nv_bfloat16>(out, out_stride, q, q_stride, k, k_stride, v, v_stride, cu_seqlens,
                                               num_tokens, B, max_seqlen, Hq, Hkv, scale, s);
