@@ -789,7 +789,7 @@ def run_prefill(args, world, rank, local):
                                f"max {int(lens.max())}), causal, Hq 28 / Hkv 4 / D 128",
                    "prompt_lengths": lens.tolist()},
         "detail": res, "vllm_fa": fa_note,
-        "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel (mma.sync m16n8k16)", "achieved": b["tflops"],
+        "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel (tcgen05.mma, TMEM accumulators, TMA)", "achieved": b["tflops"],
                      "peak": peak_tf, "unit": "TFLOP/s", "frac": b["tflops"] / peak_tf,
                      "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"},
         "cpu_baseline": {"value": cpu_tf, "unit": "TFLOP/s", "cores": 1, "kind": "port",
