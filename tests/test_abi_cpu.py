@@ -199,3 +199,26 @@ def test_tensor_segments_helper():
     assert offs.tolist() == [16, 128] and sizes.tolist() == [100, 40]
     with pytest.raises(ValueError):
         ops.tensor_segments([torch.zeros(4)], storage)
+
+
+def test_prefill_validation_on_host():
+    lib = _native.lib
+    inval, unsup = _native.AEG_ERR_INVALID_ARGUMENT, _native.AEG_ERR_UNSUPPORTED
+    buf = np.zeros(4096, np.int64)
+    p = buf.ctypes.data  # 16-byte aligned
+    args = dict(out=p, os=28 * 128, q=p, qs=28 * 128, k=p, ks=4 * 128, v=p, vs=4 * 128, cu=p, T=10, B=1, maxl=10,
+                Hq=28, Hkv=4, D=128)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return lib.aeg_prefill_attention(a["out"], a["os"], a["q"], a["qs"], a["k"], a["ks"], a["v"], a["vs"], a["cu"],
+                                         a["T"], a["B"], a["maxl"], a["Hq"], a["Hkv"], a["D"], 0.088, 0, None)
+
+    assert call(B=0) == 0 and call(T=0) == 0                   # nothing to do
+    assert call(B=-1) == inval
+    assert call(q=None) == inval
+    assert call(Hq=30) == inval                                 # not a multiple of Hkv
+    assert call(D=64) == unsup
+    assert call(qs=100) == inval                                # stride below heads x head_dim
+    assert call(q=p + 2) == inval                               # not 16-byte aligned
+    assert call(ks=4 * 128 + 4) == inval                        # stride not a multiple of 8
