@@ -28,7 +28,10 @@ Parity pins: the reference ships no kernel tests or golden vectors (its tests ar
 without numeric assertions). ``swap`` is pinned against the reference's own operator compiled
 from source into ``oracle/_ref`` (GPU test). Attention and reshape_and_cache are pinned against
 golden vectors produced by the installed vLLM's kernels of the same family
-(``tests/golden/make_golden.py``), since vLLM 0.5.1 itself is absent.
+(``tests/golden/make_golden.py``), since vLLM 0.5.1 itself is absent; so is prompt attention
+(vLLM's varlen FlashAttention, causal). ``np_step_inputs`` restates the reference's per-step
+Python loops; the reference's ``Worker`` cannot be imported here, so that integer restatement is
+not pinned to the reference's own outputs.
 """
 from __future__ import annotations
 

@@ -8,7 +8,8 @@ block table). This script runs the same kernel family from the installed vLLM 0.
 (Qwen2.5-7B attention: 28 query heads, 4 KV heads, head_dim 128, fp16, block size 16) and on a
 bf16 GQA-8 case, over per-layer views of Aegaeon's interleaved (N, L, 2, 16, Hkv, D) cache, and
 saves the inputs, vLLM's attention output and the SHA-256 of the cache after vLLM's write to
-``tests/golden/*.npz``.
+``tests/golden/*.npz``. The prompt cases run ``flash_attn_varlen_func(..., causal=True)`` on the
+q/k/v of whole prompts (the backend's prompt call) and save inputs and output.
 
 Run on a CUDA machine with vLLM installed:  python tests/golden/make_golden.py
 Only this generator touches vLLM; the tests read the saved arrays.
@@ -83,9 +84,38 @@ def _case(name, B, Hq, Hkv, ctx_lo, ctx_hi, n_blocks, L, dtype, seed, out_dir):
     print("wrote", path)
 
 
+def _prefill_case(name, lens, Hq, Hkv, dtype, seed, out_dir):
+    """Prompt attention: vLLM's varlen FlashAttention on q/k/v of whole prompts, causal (the call
+    the reference's backend makes for prompts, Aegaeon prefilling without chunking)."""
+    from vllm.vllm_flash_attn import flash_attn_varlen_func
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(seed)
+    T, D = int(sum(lens)), 128
+    q = torch.randn((T, Hq, D), generator=g).to(dtype)
+    k = torch.randn((T, Hkv, D), generator=g).to(dtype)
+    v = torch.randn((T, Hkv, D), generator=g).to(dtype)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    scale = 1.0 / math.sqrt(D)
+    out = flash_attn_varlen_func(q=q.to(dev), k=k.to(dev), v=v.to(dev), cu_seqlens_q=cu.to(dev),
+                                 cu_seqlens_k=cu.to(dev), max_seqlen_q=max(lens), max_seqlen_k=max(lens),
+                                 softmax_scale=scale, causal=True, fa_version=2)
+    torch.cuda.synchronize()
+    u16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    path = os.path.join(out_dir, f"{name}.npz")
+    np.savez_compressed(
+        path, q=u16(q), k=u16(k), v=u16(v), cu_seqlens=cu.numpy(), out_vllm=u16(out.cpu()),
+        dtype=np.array("bf16" if dtype == torch.bfloat16 else "fp16"), scale=np.float64(scale),
+        generator=np.array("vllm %s vllm_flash_attn.flash_attn_varlen_func(causal=True, fa_version=2)"
+                           % __import__("vllm").__version__))
+    print("wrote", path)
+
+
 def main(out_dir: str = HERE) -> None:
     _case("vllm_cfg1_fp16", 4, 28, 4, 17, 300, 64, 1, torch.float16, 0, out_dir)
     _case("vllm_gqa8_bf16", 6, 32, 4, 1, 400, 160, 1, torch.bfloat16, 1, out_dir)
+    _prefill_case("vllm_prefill_fp16", [1, 17, 65, 130], 4, 1, torch.float16, 2, out_dir)
+    _prefill_case("vllm_prefill_bf16", [1, 17, 65, 130], 4, 1, torch.bfloat16, 3, out_dir)
 
 
 if __name__ == "__main__":
