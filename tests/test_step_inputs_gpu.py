@@ -95,3 +95,15 @@ def test_invalid_requests_and_overflow_are_flagged(cuda_device):
     assert int(out.num_tokens.item()) == 42
     assert out.slot_mapping.cpu().tolist() == want["slot_mapping"][:10].tolist()
     assert ops.read_device_errors(cuda_device) & 0x2
+
+
+def test_out_of_range_table_updates_are_skipped_and_flagged(cuda_device):
+    bt = torch.zeros((4, 8), dtype=torch.int32, device=cuda_device)
+    ops.read_device_errors(cuda_device)
+    ops.update_block_tables(bt, [(0, 1, 7), (4, 0, 9), (1, 8, 5), (-1, 0, 3), (3, 7, 11)])
+    torch.cuda.synchronize()
+    want = torch.zeros((4, 8), dtype=torch.int32)
+    want[0, 1] = 7
+    want[3, 7] = 11
+    assert torch.equal(bt.cpu(), want)
+    assert ops.read_device_errors(cuda_device) & 0x1
