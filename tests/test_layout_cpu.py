@@ -83,3 +83,12 @@ def test_sharding_partitions_sequences(world):
         assert sh.num_blocks == sh.total_blocks  # pool sized to its own sequences
         seen.extend(sh.seq_ids.tolist())
     assert sorted(seen) == list(range(cfg.batch))
+
+
+def test_weight_switch_workload_is_qwen2_7b():
+    from aegaeon_b200 import synth
+
+    sizes = synth.qwen2_7b_param_bytes()
+    assert len(sizes) == 2 + 28 * 12 + 1           # embeddings, 12 tensors per layer, final norm, lm head
+    assert sum(sizes) == 15_231_233_024             # 7.6B bf16 parameters
+    assert sizes[0] == sizes[-1] == 152064 * 3584 * 2
