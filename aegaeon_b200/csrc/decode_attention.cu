@@ -1360,16 +1360,24 @@ cudaLaunchAttribute pdl_attr() {
   return a;
 }
 
+// Checks that the attention kernel can be configured on the current device and that its grid
+// fits the workspace's worker-warp capacity; enqueues nothing.
 template <typename T, int NT>
-int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream) {
+int check_attn_t(int max_warps) {
   const int per_sm = attn_ctas_per_sm<T, NT>();
   if (per_sm < 1) {
     (void)cudaGetLastError();
     return set_error(AEG_ERR_CUDA, "decode attention kernel cannot be configured on this device");
   }
-  if (num_sms() * per_sm * kWarps > prm.max_warps)
+  if (num_sms() * per_sm * kWarps > max_warps)
     return set_error(AEG_ERR_UNSUPPORTED, "decode: %d worker warps exceed the workspace's %d", num_sms() * per_sm * kWarps,
-                     prm.max_warps);
+                     max_warps);
+  return AEG_OK;
+}
+
+template <typename T, int NT>
+int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream) {
+  const int per_sm = attn_ctas_per_sm<T, NT>();
   // One CTA per SM (the occupancy limit), so all CTAs of the grid are resident together once the
   // preceding kernels have left the SMs; the split merge's waits on other CTAs rely on that.
   // Not a cooperative launch: a cooperative grid does not start early under programmatic
@@ -1421,18 +1429,23 @@ bool take_plan_fresh(const void* ws) {
   return g_fresh_plans.erase(ws) > 0;
 }
 
-int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_new,
-                  int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
-                  int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
-                  const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
-                  size_t workspace_bytes, void* stream, bool fuse, int flags = 0, const WsLayout* layout = nullptr) {
-  int st = validate_shape(B, Hq, Hkv, D, table_stride);
-  if (st != AEG_OK) return st;
-  if (B == 0) return AEG_OK;
+// Everything an attention launch needs, checked and built on the host before anything is
+// enqueued: the K/V tensor maps and the kernel parameters (plan_ready is set by the caller).
+struct DecodeLaunch {
+  CUtensorMap km, vm;
+  AttnParams prm;
+  int dtype;
+  int nt;
+};
+
+int decode_prepare(DecodeLaunch* dl, void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                   const void* k_new, int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache,
+                   void* v_cache, int64_t block_stride, int64_t num_blocks, const int32_t* block_tables,
+                   int table_stride, const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype,
+                   void* workspace, size_t workspace_bytes, bool fuse, int flags, const WsLayout& L) {
   AEG_CHECK_ARG(dtype == AEG_DTYPE_FP16 || dtype == AEG_DTYPE_BF16, "decode: dtype %d is not fp16/bf16", dtype);
   AEG_CHECK_ARG(out && q && k_cache && v_cache && block_tables && seq_lens, "decode: null pointer");
   AEG_CHECK_ARG(workspace != nullptr && aligned(workspace, 256), "decode: workspace must be 256-byte aligned");
-  const WsLayout L = layout ? *layout : ws_layout(B, Hq, Hkv, D);
   AEG_CHECK_ARG(workspace_bytes >= L.total, "decode: workspace of %zu bytes, need %zu", workspace_bytes, L.total);
   AEG_CHECK_ARG(num_blocks > 0 && num_blocks <= 0x7fffffffLL, "decode: num_blocks %lld out of range", (long long)num_blocks);
   AEG_CHECK_ARG(aligned(k_cache, 16) && aligned(v_cache, 16), "decode: K/V cache bases must be 16-byte aligned");
@@ -1449,14 +1462,18 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
     AEG_CHECK_ARG(aligned(k_new, 4) && aligned(v_new, 4) && k_new_stride % 2 == 0 && v_new_stride % 2 == 0,
                   "decode_layer: key/value must be 4-byte aligned with even token strides");
   }
-
-  CUtensorMap km, vm;
-  st = encode_kv_map(&km, k_cache, dtype, Hkv, block_stride, num_blocks);
+  const int nt = Hq / Hkv <= 8 ? 1 : 2;
+  int st = dtype == AEG_DTYPE_BF16 ? (nt == 1 ? check_attn_t<__nv_bfloat16, 1>(L.max_warps)
+                                               : check_attn_t<__nv_bfloat16, 2>(L.max_warps))
+                                   : (nt == 1 ? check_attn_t<__half, 1>(L.max_warps) : check_attn_t<__half, 2>(L.max_warps));
   if (st != AEG_OK) return st;
-  st = encode_kv_map(&vm, v_cache, dtype, Hkv, block_stride, num_blocks);
+  st = encode_kv_map(&dl->km, k_cache, dtype, Hkv, block_stride, num_blocks);
+  if (st != AEG_OK) return st;
+  st = encode_kv_map(&dl->vm, v_cache, dtype, Hkv, block_stride, num_blocks);
   if (st != AEG_OK) return st;
 
-  AttnParams prm{};
+  AttnParams& prm = dl->prm;
+  prm = AttnParams{};
   prm.out = out;
   prm.out_stride = out_stride;
   prm.q = q;
@@ -1473,7 +1490,7 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   prm.num_blocks = num_blocks;
   prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
   prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
-  prm.plan_ready = take_plan_fresh(workspace) ? 0 : 1;
+  prm.plan_ready = 0;
   prm.prefetch_kv = (flags & AEG_DECODE_PREFETCH) ? 1 : 0;
   prm.fuse_write = fuse ? 1 : 0;
   prm.k_new = k_new;
@@ -1484,11 +1501,33 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
   prm.v_cache = v_cache;
   prm.block_stride = block_stride;
   prm.ws = ws_ptrs(workspace, L);
-  const int nt = prm.G <= 8 ? 1 : 2;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == AEG_DTYPE_BF16)
-    return nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(km, vm, prm, s) : launch_attn_t<__nv_bfloat16, 2>(km, vm, prm, s);
-  return nt == 1 ? launch_attn_t<__half, 1>(km, vm, prm, s) : launch_attn_t<__half, 2>(km, vm, prm, s);
+  dl->dtype = dtype;
+  dl->nt = nt;
+  return AEG_OK;
+}
+
+int decode_launch(const DecodeLaunch& dl, cudaStream_t s) {
+  if (dl.dtype == AEG_DTYPE_BF16)
+    return dl.nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(dl.km, dl.vm, dl.prm, s)
+                      : launch_attn_t<__nv_bfloat16, 2>(dl.km, dl.vm, dl.prm, s);
+  return dl.nt == 1 ? launch_attn_t<__half, 1>(dl.km, dl.vm, dl.prm, s) : launch_attn_t<__half, 2>(dl.km, dl.vm, dl.prm, s);
+}
+
+int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_new,
+                  int64_t k_new_stride, const void* v_new, int64_t v_new_stride, void* k_cache, void* v_cache,
+                  int64_t block_stride, int64_t num_blocks, const int32_t* block_tables, int table_stride,
+                  const int32_t* seq_lens, int B, int Hq, int Hkv, int D, float scale, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream, bool fuse, int flags) {
+  int st = validate_shape(B, Hq, Hkv, D, table_stride);
+  if (st != AEG_OK) return st;
+  if (B == 0) return AEG_OK;
+  DecodeLaunch dl;
+  st = decode_prepare(&dl, out, out_stride, q, q_stride, k_new, k_new_stride, v_new, v_new_stride, k_cache, v_cache,
+                      block_stride, num_blocks, block_tables, table_stride, seq_lens, B, Hq, Hkv, D, scale, dtype,
+                      workspace, workspace_bytes, fuse, flags, ws_layout(B, Hq, Hkv, D));
+  if (st != AEG_OK) return st;
+  dl.prm.plan_ready = take_plan_fresh(workspace) ? 0 : 1;
+  return decode_launch(dl, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1511,9 +1550,13 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
 //     x 7 query heads each. A call that would need more is rejected with
 //     AEG_ERR_INVALID_ARGUMENT before anything is enqueued.
 //   * Nothing in the scratch has to start at zero for the first call: the plan kernel that
-//     every call enqueues writes the whole header, including the barrier counters that the
-//     attention kernel needs at zero, and the last warp of the attention kernel sets them back
-//     to zero. (Static device memory also starts zeroed when the module is loaded.)
+//     every call enqueues rewrites the header, the warp, unit, split-pair and merge records,
+//     and sets every CTA's publication flag to zero. The attention kernel then stamps each
+//     CTA's flag with (its value at launch) + 1 once that CTA's partials are stored, and the
+//     merge waits for that stamp; the partial rows are written before they are read. (Static
+//     device memory also starts zeroed when the module is loaded.)
+//   * A call that fails a check (arguments, sizes, alignment, tensor-map encoding) returns its
+//     error before enqueuing anything, so it leaves the scratch as the previous call left it.
 //   * One scratch per device means calls on one device must not overlap: two calls in flight
 //     at once on different streams race on the plan, the counters and the partials. Issue
 //     them on one stream, or order the streams.
@@ -1631,14 +1674,19 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
   void* scratch = nullptr;
   st = aeg::noalloc_scratch(&scratch);
   if (st != AEG_OK) return st;
+  // Every argument check, the kernel configuration and the tensor maps come before the first
+  // launch: a rejected call enqueues nothing and leaves the scratch as the last call left it.
+  aeg::DecodeLaunch dl;
+  st = aeg::decode_prepare(&dl, out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
+                           const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
+                           Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, false, 0, L);
+  if (st != AEG_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W,
                                                           aeg::ws_ptrs(scratch, L));
   AEG_CHECK_LAUNCH("decode_plan (noalloc)");
-  aeg::mark_plan_fresh(scratch);
-  return aeg::decode_common(out, out_stride, q, q_stride, nullptr, 0, nullptr, 0, const_cast<void*>(k_cache),
-                            const_cast<void*>(v_cache), block_stride, num_blocks, block_tables, table_stride, seq_lens, B,
-                            Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, stream, false, 0, &L);
+  dl.prm.plan_ready = 0;  // the plan kernel directly precedes this launch: read it after the wait
+  return aeg::decode_launch(dl, s);
 }
 
 }  // extern "C"

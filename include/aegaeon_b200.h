@@ -330,7 +330,9 @@ AEG_API int aeg_decode_layer(void* out, int64_t out_stride, const void* q, int64
  *     Hq/Hkv = 7, 20 MB at 16, on a 148-SM B200) plus 48 bytes per (sequence, KV head) pair; a
  *     call needing more than 32 MiB (over ~500K pairs at Hq/Hkv = 7, ~280K at 16) fails with
  *     AEG_ERR_INVALID_ARGUMENT, nothing enqueued.
- *   - Nothing has to be zeroed by the caller: every call re-plans and resets the counters it uses.
+ *   - Every check (arguments, alignment, tensor maps) runs before the first launch: a call that
+ *     returns an error has enqueued nothing and left the scratch as the previous call left it.
+ *   - Nothing has to be zeroed by the caller: every call re-plans and resets the flags it uses.
  *   - The scratch is shared by all calls on a device: calls that overlap in time (e.g. on two
  *     unordered streams) race. Keep them on one stream or order them.
  *   - The first call on a device looks up the scratch address and configures the kernel with that

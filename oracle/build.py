@@ -22,7 +22,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_MODULE = "aegaeon_ref_ops"
-REFERENCE_OPS_DIR = os.environ.get("AEGAEON_REFERENCE_OPS", "/root/reference/aegaeon/ops")
+# The reference checkout is expected beside this repository (``<parent>/reference/aegaeon/ops``);
+# AEGAEON_REFERENCE_OPS names another location of the reference's ``aegaeon/ops`` directory.
+REFERENCE_OPS_DIR = os.environ.get(
+    "AEGAEON_REFERENCE_OPS",
+    os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "aegaeon", "ops"))
 
 
 def build_oracle_lib(force: bool = False) -> str:

@@ -2,8 +2,10 @@
 
 Both are called through the C ABI on the same inputs: the regular path as aeg_decode_plan +
 aeg_paged_attn_decode with a caller-owned workspace, the allocation-free one with no workspace.
-Two calls in a row with different batches check that the static scratch is re-planned and its
-counters reset between calls. The file name sorts last so that the suite also runs it after
+They run the same plan and kernel, so their outputs must be equal bit for bit; one case is also
+checked against the oracle. Two calls in a row with different batches check that the static
+scratch is re-planned and its flags reset between calls, and a rejected call must enqueue
+nothing. The file name sorts last so that the suite also runs it after
 every other GPU test; it passes on its own in a fresh process too.
 """
 import ctypes
@@ -14,8 +16,7 @@ import torch
 
 from aegaeon_b200 import _native
 from aegaeon_b200._native import AEG_DTYPE_BF16, AEG_DTYPE_FP16, AEG_ERR_INVALID_ARGUMENT, AEG_OK
-from oracle import oracle as orc
-from tests.gpu_helpers import ATOL, RTOL, DT, decode_case
+from tests.gpu_helpers import assert_attention_close, decode_case, oracle_attention_layer
 
 pytestmark = pytest.mark.gpu
 
@@ -69,6 +70,9 @@ def _case(seed, B, Hq, Hkv, dtype, max_len):
 
 
 def test_noalloc_matches_regular_entry_on_two_calls_in_a_row(cuda_device):
+    # Both entries run the same plan (the same worker count, hence the same cuts) and the same
+    # kernel, so their outputs must agree bit for bit; the first case is also held to the
+    # oracle's attention tolerance.
     stream = torch.cuda.current_stream().cuda_stream
     cases = [_case(11, 64, 28, 4, torch.float16, 3000), _case(12, 24, 32, 8, torch.bfloat16, 1800)]
     outs = []
@@ -78,11 +82,33 @@ def test_noalloc_matches_regular_entry_on_two_calls_in_a_row(cuda_device):
     for (kv, q, tables, sl), got in zip(cases, outs):
         want = _regular(q, kv, 1, tables, sl, stream)
         torch.cuda.synchronize()
-        ok, err, excess = orc.compare_attention(_bits(got), _bits(want), DT[q.dtype], ATOL, RTOL)
-        assert ok, f"noalloc vs regular ({q.dtype}): max |err| {err:.3e}, excess {excess:.3e}"
+        g, w = _bits(got), _bits(want)
+        assert np.array_equal(g, w), f"noalloc vs regular ({q.dtype}): {int((g != w).sum())} elements differ"
+    kv, q, tables, sl = cases[0]
+    want = oracle_attention_layer(q, kv[:, 1, 0], kv[:, 1, 1], tables.cpu().numpy(), sl.cpu().numpy(), SCALE)
+    assert_attention_close(outs[0], want, "noalloc vs oracle")
     flags = ctypes.c_uint32(0)
     assert LIB.aeg_read_device_errors(stream, ctypes.byref(flags)) == AEG_OK
     assert flags.value == 0
+
+
+def test_noalloc_rejected_call_enqueues_nothing(cuda_device):
+    # A call that fails a check made after the scratch lookup (here num_blocks = 0) returns the
+    # error before launching anything: its output is untouched and the next call still matches
+    # the regular entry bit for bit.
+    stream = torch.cuda.current_stream().cuda_stream
+    kv, q, tables, sl = _case(13, 16, 28, 4, torch.float16, 900)
+    out = torch.full_like(q, 7.0)
+    args = _args(out, q, kv, 0, tables, sl)
+    args[7] = 0  # num_blocks
+    assert LIB.aeg_paged_attn_decode_noalloc(*args, stream) == AEG_ERR_INVALID_ARGUMENT
+    assert "num_blocks" in _native.last_error()
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
+    got = _noalloc(q, kv, 0, tables, sl, stream)
+    want = _regular(q, kv, 0, tables, sl, stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(got), _bits(want))
 
 
 def test_noalloc_rejects_a_batch_beyond_the_scratch(cuda_device):
