@@ -1375,8 +1375,11 @@ int check_attn_t(int max_warps) {
   return AEG_OK;
 }
 
+// `started` (may be null): an event that fires once every CTA of this launch has started
+// (programmatic event triggered at block start); see LaunchOrder.
 template <typename T, int NT>
-int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream) {
+int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams& prm, cudaStream_t stream,
+                  cudaEvent_t started) {
   const int per_sm = attn_ctas_per_sm<T, NT>();
   // One CTA per SM (the occupancy limit), so all CTAs of the grid are resident together once the
   // preceding kernels have left the SMs; the split merge's waits on other CTAs rely on that.
@@ -1384,14 +1387,22 @@ int launch_attn_t(const CUtensorMap& km, const CUtensorMap& vm, const AttnParams
   // dependent launch (measured: cfg2 step 0.506 -> 0.439 ms without it). The next layer's grid
   // cannot take SMs before every CTA of this one has started (it launches only when all of them
   // have passed griddepcontrol.launch_dependents), and every wait is bounded.
-  cudaLaunchAttribute attr[1] = {pdl_attr()};
+  cudaLaunchAttribute attr[2] = {pdl_attr(), cudaLaunchAttribute{}};
+  unsigned n_attr = 1;
+  if (started != nullptr) {
+    attr[1].id = cudaLaunchAttributeProgrammaticEvent;
+    attr[1].val.programmaticEvent.event = started;
+    attr[1].val.programmaticEvent.flags = 0;
+    attr[1].val.programmaticEvent.triggerAtBlockStart = 1;
+    n_attr = 2;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms() * per_sm));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = AttnSmem<NT>::kDynamic;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n_attr;
   AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, decode_attn_kernel<T, NT>, km, vm, prm));
   return AEG_OK;
 }
@@ -1506,11 +1517,84 @@ int decode_prepare(DecodeLaunch* dl, void* out, int64_t out_stride, const void* 
   return AEG_OK;
 }
 
-int decode_launch(const DecodeLaunch& dl, cudaStream_t s) {
+// Order of attention launches on one device across streams.
+//
+// The split merge waits for other CTAs of its own grid, which is safe only if the whole grid is
+// resident together. On one stream that holds: a launch starts only when every CTA of the
+// previous one has started (programmatic dependent launch) or that kernel has finished. Two
+// grids on two streams could each hold part of the SMs and wait for CTAs that cannot start
+// until the other grid leaves; the bounded waits would then time out. So every eager launch
+// carries a programmatic event that fires once all of its CTAs have started, and a launch on a
+// different stream than the device's previous attention launch first waits for that event (as
+// a programmatic dependency: its CTAs may start early but proceed past griddepcontrol.wait only
+// when that grid has finished). Each grid therefore starts only after the previous one is fully
+// resident, so at most one grid is ever partially resident and every wait ends. Launches made
+// while a stream is being captured into a CUDA graph are not ordered this way: graphs that
+// hold attention launches must be replayed on one stream or on streams the caller orders.
+class LaunchOrder {
+ public:
+  ~LaunchOrder() { if (locked_) mu_of(dev_).unlock(); }
+
+  // Locks the device's order and, if needed, makes `s` wait for the previous launch's start.
+  // On return event() is the event to attach to the launch (null when not ordering).
+  int enter(cudaStream_t s, bool* waited) {
+    *waited = false;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    AEG_CHECK_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return AEG_OK;
+    AEG_CHECK_CUDA(cudaGetDevice(&dev_));
+    if (dev_ < 0 || dev_ >= kDevices)
+      return set_error(AEG_ERR_UNSUPPORTED, "decode: device ordinal %d >= %d", dev_, kDevices);
+    mu_of(dev_).lock();
+    locked_ = true;
+    State& st = state()[dev_];
+    if (st.started == nullptr) AEG_CHECK_CUDA(cudaEventCreateWithFlags(&st.started, cudaEventDisableTiming));
+    if (st.any && st.last != s) {
+      AEG_CHECK_CUDA(cudaStreamWaitEvent(s, st.started, 0));
+      *waited = true;
+    }
+    stream_ = s;
+    return AEG_OK;
+  }
+  cudaEvent_t event() const { return locked_ ? state()[dev_].started : nullptr; }
+  // Records that the launch carrying event() was made on the stream given to enter().
+  void launched() {
+    if (!locked_) return;
+    State& st = state()[dev_];
+    st.last = stream_;
+    st.any = true;
+  }
+
+ private:
+  static constexpr int kDevices = 64;
+  struct State {
+    cudaEvent_t started = nullptr;
+    cudaStream_t last = nullptr;
+    bool any = false;
+  };
+  static State* state() {
+    static State s[kDevices];
+    return s;
+  }
+  static std::mutex& mu_of(int dev) {
+    static std::mutex m[kDevices];
+    return m[dev];
+  }
+  int dev_ = -1;
+  bool locked_ = false;
+  cudaStream_t stream_ = nullptr;
+};
+
+int decode_launch(const DecodeLaunch& dl, cudaStream_t s, LaunchOrder& order) {
+  cudaEvent_t ev = order.event();
+  int st;
   if (dl.dtype == AEG_DTYPE_BF16)
-    return dl.nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(dl.km, dl.vm, dl.prm, s)
-                      : launch_attn_t<__nv_bfloat16, 2>(dl.km, dl.vm, dl.prm, s);
-  return dl.nt == 1 ? launch_attn_t<__half, 1>(dl.km, dl.vm, dl.prm, s) : launch_attn_t<__half, 2>(dl.km, dl.vm, dl.prm, s);
+    st = dl.nt == 1 ? launch_attn_t<__nv_bfloat16, 1>(dl.km, dl.vm, dl.prm, s, ev)
+                    : launch_attn_t<__nv_bfloat16, 2>(dl.km, dl.vm, dl.prm, s, ev);
+  else
+    st = dl.nt == 1 ? launch_attn_t<__half, 1>(dl.km, dl.vm, dl.prm, s, ev) : launch_attn_t<__half, 2>(dl.km, dl.vm, dl.prm, s, ev);
+  if (st == AEG_OK) order.launched();
+  return st;
 }
 
 int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_new,
@@ -1526,8 +1610,16 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
                       block_stride, num_blocks, block_tables, table_stride, seq_lens, B, Hq, Hkv, D, scale, dtype,
                       workspace, workspace_bytes, fuse, flags, ws_layout(B, Hq, Hkv, D));
   if (st != AEG_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchOrder order;
+  bool waited = false;
+  st = order.enter(s, &waited);
+  if (st != AEG_OK) return st;
   dl.prm.plan_ready = take_plan_fresh(workspace) ? 0 : 1;
-  return decode_launch(dl, static_cast<cudaStream_t>(stream));
+  // After a wait for another stream's grid, that grid is a programmatic predecessor of this
+  // launch too: request no tiles before the grid-dependency wait.
+  if (waited) dl.prm.prefetch_kv = 0;
+  return decode_launch(dl, s, order);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1682,11 +1774,15 @@ int aeg_paged_attn_decode_noalloc(void* out, int64_t out_stride, const void* q, 
                            Hq, Hkv, D, scale, dtype, scratch, aeg::kNoAllocScratchBytes, false, 0, L);
   if (st != AEG_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  aeg::LaunchOrder order;
+  bool waited = false;
+  st = order.enter(s, &waited);
+  if (st != AEG_OK) return st;
   aeg::decode_plan_kernel<<<1, aeg::kPlanThreads, 0, s>>>(seq_lens, block_tables, B, Hkv, Hq / Hkv, table_stride, W,
                                                           aeg::ws_ptrs(scratch, L));
   AEG_CHECK_LAUNCH("decode_plan (noalloc)");
   dl.prm.plan_ready = 0;  // the plan kernel directly precedes this launch: read it after the wait
-  return aeg::decode_launch(dl, s);
+  return aeg::decode_launch(dl, s, order);
 }
 
 }  // extern "C"
