@@ -15,12 +15,25 @@ __device__ unsigned int g_deverr_cache = 0;
 
 constexpr int kCacheThreads = 128;
 
+// Both kernels run under programmatic dependent launch: they wait for the preceding kernel
+// (which may have produced the keys, values or slots) and then let the next kernel launch, so
+// that their launch latency and the next kernel's overlap the work before them. Each thread
+// issues its first row loads together with the slot load, so a token costs one global round
+// trip before its stores.
 __global__ void __launch_bounds__(kCacheThreads)
 reshape_and_cache_vec_kernel(const uint4* __restrict__ key, const uint4* __restrict__ value, int64_t key_stride_v,
                              int64_t value_stride_v, uint4* __restrict__ k_cache, uint4* __restrict__ v_cache,
                              int64_t block_stride_v, int64_t num_slots, const int64_t* __restrict__ slot_mapping,
                              int row_vecs) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int64_t t = blockIdx.x;
+  const int i0 = threadIdx.x;
+  uint4 first = make_uint4(0u, 0u, 0u, 0u);
+  if (i0 < row_vecs)
+    first = key[t * key_stride_v + i0];
+  else if (i0 < 2 * row_vecs)
+    first = value[t * value_stride_v + i0 - row_vecs];
   const int64_t slot = slot_mapping[t];
   if (slot < 0) return;
   if (slot >= num_slots) {
@@ -28,7 +41,11 @@ reshape_and_cache_vec_kernel(const uint4* __restrict__ key, const uint4* __restr
     return;
   }
   const int64_t dst = (slot >> 4) * block_stride_v + (slot & 15) * row_vecs;
-  for (int i = threadIdx.x; i < 2 * row_vecs; i += blockDim.x) {
+  if (i0 < row_vecs)
+    k_cache[dst + i0] = first;
+  else if (i0 < 2 * row_vecs)
+    v_cache[dst + i0 - row_vecs] = first;
+  for (int i = i0 + blockDim.x; i < 2 * row_vecs; i += blockDim.x) {
     if (i < row_vecs)
       k_cache[dst + i] = key[t * key_stride_v + i];
     else
@@ -42,6 +59,8 @@ reshape_and_cache_elem_kernel(const uint16_t* __restrict__ key, const uint16_t* 
                               int64_t key_stride, int64_t value_stride, uint16_t* __restrict__ k_cache,
                               uint16_t* __restrict__ v_cache, int64_t block_stride, int64_t num_slots,
                               const int64_t* __restrict__ slot_mapping, int row_elems) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int64_t t = blockIdx.x;
   const int64_t slot = slot_mapping[t];
   if (slot < 0) return;
@@ -88,16 +107,25 @@ extern "C" int aeg_reshape_and_cache(const void* key, const void* value, int64_t
   const bool vec = (row % 8 == 0) && (key_stride % 8 == 0) && (value_stride % 8 == 0) && (block_stride % 8 == 0) &&
                    aeg::aligned(key, 16) && aeg::aligned(value, 16) && aeg::aligned(k_cache, 16) &&
                    aeg::aligned(v_cache, 16);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(T));
+  cfg.blockDim = dim3(aeg::kCacheThreads);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (vec) {
-    aeg::reshape_and_cache_vec_kernel<<<static_cast<unsigned>(T), aeg::kCacheThreads, 0, s>>>(
-        static_cast<const uint4*>(key), static_cast<const uint4*>(value), key_stride / 8, value_stride / 8,
-        static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), block_stride / 8, num_slots, slot_mapping,
-        static_cast<int>(row / 8));
+    AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, aeg::reshape_and_cache_vec_kernel, static_cast<const uint4*>(key),
+                                      static_cast<const uint4*>(value), key_stride / 8, value_stride / 8,
+                                      static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), block_stride / 8,
+                                      num_slots, slot_mapping, static_cast<int>(row / 8)));
   } else {
-    aeg::reshape_and_cache_elem_kernel<<<static_cast<unsigned>(T), aeg::kCacheThreads, 0, s>>>(
-        static_cast<const uint16_t*>(key), static_cast<const uint16_t*>(value), key_stride, value_stride,
-        static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), block_stride, num_slots, slot_mapping,
-        static_cast<int>(row));
+    AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, aeg::reshape_and_cache_elem_kernel, static_cast<const uint16_t*>(key),
+                                      static_cast<const uint16_t*>(value), key_stride, value_stride,
+                                      static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), block_stride,
+                                      num_slots, slot_mapping, static_cast<int>(row)));
   }
   AEG_CHECK_LAUNCH("reshape_and_cache");
   return AEG_OK;

@@ -23,6 +23,7 @@ Other configs: cfg1/cfg2/cfg4 (decode), cfg5 (swap / copy_blocks), migrate, prep
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -55,6 +56,8 @@ def _args():
     p.add_argument("--swap-scale", type=float, default=1.0, help="decode configs: scale the swap set (small cases)")
     p.add_argument("--unfused", action="store_true",
                    help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
+    p.add_argument("--layers", type=int, default=0,
+                   help="decode configs, profiling only: override the layer count (same work per launch, smaller pool)")
     p.add_argument("--compact-pool", action="store_true",
                    help="size the block pool to the blocks the batch uses (same kernels; small-case profiling)")
     p.add_argument("--scale", type=float, default=1.0,
@@ -214,7 +217,7 @@ class CpuDecodeSample:
     that one step takes about ``target_step_s`` on this host. Each layer has its own cache
     blocks (the sample's blocks only); the values are N(0, std^2) in the storage dtype."""
 
-    MAX_SAMPLE_BYTES = 6 << 30
+    MAX_SAMPLE_BYTES = 8 << 30
 
     def __init__(self, cfg, lay, target_step_s: float, seed: int = 0):
         from oracle.torch_ref import host_threads
@@ -241,9 +244,23 @@ class CpuDecodeSample:
                 break
             k = min(B, k * 2)
         del probe, probe_step
-        self.k = k
         self.s = self._build(k, cfg.num_layers, seed)
         self.step = self._stepper(self.s, cfg.num_layers)
+        # the probe overstates the cost of a large sample (fixed per-call costs): time one real
+        # step and grow the sample once if it runs well under the target
+        t0 = time.perf_counter()
+        self.step()
+        t_step = time.perf_counter() - t0
+        if t_step < 0.5 * target_step_s and k > 1:
+            k2 = max(1, int(k * t_step / target_step_s))
+            while k2 < k and self._pick_blocks(k2) * cfg.num_layers * block_bytes > self.MAX_SAMPLE_BYTES:
+                k2 += 1
+            if k2 < k:
+                del self.s, self.step
+                k = k2
+                self.s = self._build(k, cfg.num_layers, seed)
+                self.step = self._stepper(self.s, cfg.num_layers)
+        self.k = k
         self.batch = self.s["batch"]
         self.sum_ctx = self.s["sum_ctx"]
 
@@ -581,6 +598,8 @@ def run_decode(args, world, rank, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     cfg = synth.CONFIGS[args.config]
+    if args.layers:
+        cfg = dataclasses.replace(cfg, num_layers=args.layers)
     lay, scaling = _decode_layout(cfg, world, rank)
     if args.compact_pool:
         lay = synth.compact_layout(lay)

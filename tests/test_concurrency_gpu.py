@@ -27,6 +27,15 @@ pytestmark = pytest.mark.gpu
 SLEEP_CYCLES = int(4e8)  # ~0.2 s of device time at B200 clocks
 
 
+def _warm_kernels(device):
+    """Runs once every kernel the ordering checks launch, so that no lazy module load (which waits
+    for the device) happens while the swap stream is busy."""
+    torch.cuda._sleep(1000)
+    marker = torch.ones(1, device=device)
+    marker += 1
+    torch.cuda.synchronize()
+
+
 def _pools(n_dev, n_host, seed):
     geom = layout.kv_block_shape(28, 4, 128)
     dev = synth.random_bits_(torch.empty((n_dev,) + geom, dtype=torch.float16, device="cuda"), seed)
@@ -43,7 +52,7 @@ def test_swap_out_is_ordered_on_the_current_stream(cuda_device, engine):
     # swap_sm takes its ids from device tensors staged before the stream work (a list would be
     # copied from pageable memory, which may make the host wait for the stream)
     d_src, d_dst = torch.as_tensor(src, device=cuda_device), torch.as_tensor(dst, device=cuda_device)
-    torch.cuda.synchronize()
+    _warm_kernels(cuda_device)
     before = host.view(torch.int16).clone()
     swap_stream = torch.cuda.Stream()
     with torch.cuda.stream(swap_stream):
@@ -76,6 +85,7 @@ def test_swap_in_is_ordered_on_the_current_stream(cuda_device):
     src = rng.permutation(48)[:32].tolist()
     dst = rng.permutation(64)[:32].tolist()
     before = kv.view(torch.int16).clone()
+    _warm_kernels(cuda_device)
     swap_stream = torch.cuda.Stream()
     with torch.cuda.stream(swap_stream):
         torch.cuda._sleep(SLEEP_CYCLES)
