@@ -26,6 +26,7 @@ AEG_DEVERR_WAIT_TIMEOUT = 0x8
 AEG_DEVERR_PLAN_MISMATCH = 0x10
 
 AEG_DECODE_PREFETCH = 0x1
+AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE = 0x2
 
 AEG_IPC_HANDLE_BYTES = 96
 

@@ -26,13 +26,14 @@
 //     and accumulates O^T += V^T P^T (V fragments by ldmatrix.trans). For bf16, P enters as a
 //     bf16 value plus its bf16 rounding residue (two MMAs) so that P V keeps ~16 mantissa bits.
 //   * A whole pair's unit writes the output rows; a split unit writes an fp32 partial (O scaled
-//     by 2^-max, max, sum). When its range is done the CTA's warps meet and one thread stamps
-//     the CTA's flag (its own cache line) with the launch's epoch by a release store. Every CTA
-//     stamps its flag once per launch, so all flags hold the same value between launches (the
-//     plan zeroes them) and a CTA takes the epoch from its own flag, with no end-of-launch
-//     counter. Then all warps merge the split pairs: the plan spreads the merge
-//     items evenly over the warps, and an item waits only for the flags of the CTAs that
-//     computed its pair's pieces (one CTA per SM: all CTAs are resident together). A
+//     by 2^-max, max, sum). When its range is done each worker warp stamps its own flag (its own
+//     cache line) with the launch's epoch by a release store. Every warp stamps its flag once
+//     per launch, so all flags hold the same value between launches (the plan zeroes them) and a
+//     warp takes the epoch from its own flag, with no end-of-launch counter. Then all warps merge
+//     the split pairs: the plan spreads the merge items evenly over the warps, and an item waits
+//     only for the flags of the warps that computed its pair's pieces (one CTA per SM: all CTAs
+//     are resident together; a CTA-wide publication made every merge wait for the slowest warp of
+//     each producing CTA, ~1 us). A
 //     merge item covers 4 query heads of a pair with up to 4 pieces, one head of a pair with
 //     up to 16 (in 4 lane groups), or a dimension chunk of one head beyond that, so that a lane
 //     folds at most 4 (16) pieces loaded in one round trip. Measured and rejected: signalling
@@ -81,7 +82,7 @@ constexpr int kStageBytes = 2 * kBoxBytes;
 // Header words of the workspace.
 constexpr int kHdrItems = 0, kHdrWarps = 1, kHdrUnits = 2, kHdrSplitPairs = 3, kHdrSlots = 4,
               kHdrMergeItems = 5;
-constexpr int kFlagStride = 32;  // int32 words between CTA flags: one 128-byte line each
+constexpr int kFlagStride = 32;  // int32 words between worker-warp flags: one 128-byte line each
 constexpr int kMergeBatch = 16;      // pieces a lane loads per round trip in the split merge
 constexpr int kMergeLaneGroups = 4;  // lane groups of a small merge item (heads or piece groups)
 constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item folds per round trip
@@ -92,12 +93,12 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 //   warp_rec    : int4[3 * (max_warps + 1)]  per worker warp w: {first unit, 0, 0, 0} and a copy of
 //                            its first unit's record (one load starts a warp); entry `warps`
 //                            holds the end of the unit list
-//   split_pairs : int4[P]    {pair, first partial slot, nsplit | shape << 16, first CTA | CTAs
-//                            << 16} of every (sequence, head) cut across warps (nsplit >= 2)
-//                            and {pair, 0, shape << 16, 0} of every empty one; its merge is
-//                            merge_items(shape) items, which wait for the CTAs that computed
-//                            its pieces
-//   cta_flag    : int32[max_warps / 8 * kFlagStride] per CTA (one cache line each): the
+//   split_pairs : int4[P]    {pair, first partial slot, nsplit | shape << 16, first warp |
+//                            warps << 16} of every (sequence, head) cut across warps (nsplit
+//                            >= 2) and {pair, 0, shape << 16, 0} of every empty one; its merge
+//                            is merge_items(shape) items, which wait for the worker warps that
+//                            computed its pieces
+//   warp_flag   : int32[max_warps * kFlagStride] per worker warp (one cache line each): the
 //                            number of launches with this plan whose partials it has published
 //   merge_rec   : int4[max_warps]  per warp: {split-pair entry, item within it, items, 0}, its
 //                            share of the merge items (balanced like the blocks)
@@ -106,7 +107,7 @@ constexpr int kMergeHeadBatch = 4;   // pieces a lane of a small merge item fold
 //   part_ml     : float2[max_slots * G]        (max in log2 units, sum) per query head
 //   part_o      : float [max_slots * G * D]    partial outputs, scaled by 2^-max
 struct WsLayout {
-  size_t warp_rec, split_pairs, cta_flag, merge_rec, units, part_ml, part_o, total;
+  size_t warp_rec, split_pairs, warp_flag, merge_rec, units, part_ml, part_o, total;
   int max_warps, max_units, max_slots;
 };
 
@@ -126,8 +127,8 @@ WsLayout layout_for(int B, int Hq, int Hkv, int D, int max_warps) {
   off = align256(off + 3 * sizeof(int4) * size_t(max_warps + 1));
   w.split_pairs = off;
   off = align256(off + sizeof(int4) * P);
-  w.cta_flag = off;
-  off = align256(off + sizeof(int) * size_t(max_warps / kWarps) * kFlagStride);
+  w.warp_flag = off;
+  off = align256(off + sizeof(int) * size_t(max_warps) * kFlagStride);
   w.merge_rec = off;
   off = align256(off + sizeof(int4) * size_t(max_warps));
   w.units = off;
@@ -146,7 +147,7 @@ struct WsPtrs {
   int* header;
   int4* warp_rec;
   int4* split_pairs;
-  int* cta_flag;
+  int* warp_flag;
   int4* merge_rec;
   int4* units;
   float2* part_ml;
@@ -156,7 +157,7 @@ struct WsPtrs {
 inline WsPtrs ws_ptrs(void* ws, const WsLayout& L) {
   char* b = static_cast<char*>(ws);
   return WsPtrs{reinterpret_cast<int*>(b), reinterpret_cast<int4*>(b + L.warp_rec),
-                reinterpret_cast<int4*>(b + L.split_pairs), reinterpret_cast<int*>(b + L.cta_flag),
+                reinterpret_cast<int4*>(b + L.split_pairs), reinterpret_cast<int*>(b + L.warp_flag),
                 reinterpret_cast<int4*>(b + L.merge_rec),
                 reinterpret_cast<int4*>(b + L.units),
                 reinterpret_cast<float2*>(b + L.part_ml), reinterpret_cast<float*>(b + L.part_o)};
@@ -312,7 +313,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     }
     for (int w = tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(0, 0, 0, 0);
     for (int w = tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(0, 0, 0, 0);
-    for (int c = tid; c < W / kWarps; c += kPlanThreads) ws.cta_flag[c * kFlagStride] = 0;
+    for (int c = tid; c < W; c += kPlanThreads) ws.warp_flag[c * kFlagStride] = 0;
     return;
   }
   const int Wp = I < W ? static_cast<int>(I) : W;  // workers with items; their starts are distinct
@@ -367,7 +368,7 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
     ws.header[kHdrSlots] = SL;
     ws.header[kHdrMergeItems] = static_cast<int>(MI < 0x7fffffffLL ? MI : 0x7fffffffLL);
   }
-  for (int c = tid; c < W / kWarps; c += kPlanThreads) ws.cta_flag[c * kFlagStride] = 0;
+  for (int c = tid; c < W; c += kPlanThreads) ws.warp_flag[c * kFlagStride] = 0;
   for (int w = Wp + tid; w <= W; w += kPlanThreads) ws.warp_rec[3 * w] = make_int4(U, 0, 0, 0);  // empty ranges
   for (int w = Wm + tid; w < W; w += kPlanThreads) ws.merge_rec[w] = make_int4(S, 0, 0, 0);      // no merge items
 
@@ -412,9 +413,9 @@ decode_plan_kernel(const int* __restrict__ seq_lens, const int* __restrict__ tab
       const int shape = merge_shape(c + 1, G), n_it = merge_items(shape, G);
       mark_merge(sp, mo, n_it);
       mo += n_it;
-      const int cta0 = static_cast<int>((wk.le(ob) - 1) / kWarps);
-      const int cta1 = static_cast<int>((wk.le(ob + nb - 1) - 1) / kWarps);
-      ws.split_pairs[sp++] = make_int4(p, slot, (c + 1) | (shape << 16), cta0 | ((cta1 - cta0 + 1) << 16));
+      const int w0 = static_cast<int>(wk.le(ob) - 1);           // worker holding the first block
+      const int w1 = static_cast<int>(wk.le(ob + nb - 1) - 1);  // and the last
+      ws.split_pairs[sp++] = make_int4(p, slot, (c + 1) | (shape << 16), w0 | ((w1 - w0 + 1) << 16));
     }
     int queued = -1;
     if (c + 1 > kPlanLongUnits) {
@@ -481,6 +482,10 @@ struct AttnParams {
   // Fused cache write (decode_layer): the new token of sequence b (position seq_len - 1) is
   // written into the cache and patched into the tile that holds it.
   int fuse_write;
+  // The preceding kernel may have written the newest position (seq_len - 1) of each sequence
+  // (the decode cache write) and nothing else this launch reads: tiles may be requested early,
+  // and each sequence's newest row is read again after the grid-dependency wait and patched in.
+  int refresh_last;
   const void* k_new;
   const void* v_new;
   int64_t k_new_stride;  // token strides of k_new / v_new (elements)
@@ -515,6 +520,12 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -726,18 +737,18 @@ __device__ __forceinline__ void merge_item(const AttnParams& p, const int4& e, i
 // A split-pair entry is used only if it fits this call's shape (see unit_items).
 __device__ __forceinline__ bool entry_ok(const int4& e, const AttnParams& p) {
   const int shape = e.z >> 16, q = shape & 0xff, hg = shape >> 8, ns = e.z & 0xffff;
-  const int cta0 = e.w & 0xffff, n_ctas = e.w >> 16;
+  const int w0 = e.w & 0xffff, n_w = e.w >> 16;
   const bool shape_ok = (q == 1 && hg == 4 && ns <= 4) || (q == 1 && hg == 1 && ns > 4 && ns <= kMergeBatch) ||
                         (hg == 1 && (q == 2 || q == 4 || q == 8 || q == 16 || q == 32));
   return e.x >= 0 && e.x < p.num_pairs && e.y >= 0 && e.y + ns <= p.max_slots && shape_ok &&
-         cta0 + n_ctas <= static_cast<int>(gridDim.x) && (ns == 0) == (n_ctas == 0);
+         w0 + n_w <= static_cast<int>(gridDim.x) * kWarps && (ns == 0) == (n_w == 0);
 }
 
 __device__ __forceinline__ void st_release_gpu(int* p, int v) {
   asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Waits until *flag == v (a CTA's publication stamp), for at most kWaitLimitNs.
+// Waits until *flag == v (a worker warp's publication stamp), for at most kWaitLimitNs.
 __device__ __forceinline__ bool flag_wait(const int* flag, int v) {
   if (ld_acquire_gpu(flag) == v) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -998,11 +1009,13 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     pdl_wait_primary();
     pdl_launch_dependents();
   }
-  // Launches with this plan so far: this CTA's own flag, which every CTA of every earlier launch
-  // stamped once (written by the previous launch, read after waiting for it).
-  const int epoch_word = lane == 0 ? ld_acquire_gpu(&p.ws.cta_flag[blockIdx.x * kFlagStride]) : 0;
   if (n_units > 0) load_q(0);
   refill();
+  // Launches with this plan so far: this warp's own flag, which every worker warp of every
+  // earlier launch stamped once. The previous launch wrote it and has finished (the wait above),
+  // so a relaxed load sees it; issued after the first tiles, it delays nothing, and its value
+  // is needed only when this warp publishes.
+  const int epoch_word = lane == 0 ? ld_relaxed_gpu(&p.ws.warp_flag[gw * kFlagStride]) : 0;
 
   for (int c = 0; c < n_units; ++c) {
     if (c > 0 && lane == ((c - 1) & 31) && c + 31 < n_units) {
@@ -1045,10 +1058,24 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     if (c + 1 < n_units) load_q(c + 1);
     if (n == 0) continue;
 
-    // Fused cache write: this unit reads the block of position n_ctx - 1.
-    const bool last = p.fuse_write && n_ctx > 0 && j0 + n == (n_ctx + kBlockTokens - 1) / kBlockTokens;
+    // Fused cache write (or the refresh of a row written just before): this unit reads the block
+    // of position n_ctx - 1.
+    const bool last = (p.fuse_write || p.refresh_last) && n_ctx > 0 &&
+                      j0 + n == (n_ctx + kBlockTokens - 1) / kBlockTokens;
     uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
-    if (last) {
+    if (last && !p.fuse_write) {
+      // The newest row of head h as the preceding kernel left it (read after the wait, through
+      // L2); the block id comes from the unit record when it holds it, else from the table.
+      const int il = n - 1;
+      const int blk = il == 0 ? ub.y : il == 1 ? ub.z : il == 2 ? ub.w
+                    : p.tables[static_cast<int64_t>(b) * p.table_stride + (n_ctx - 1) / kBlockTokens];
+      if (static_cast<unsigned long long>(static_cast<long long>(blk)) < static_cast<unsigned long long>(p.num_blocks)) {
+        const int64_t off = static_cast<int64_t>(blk) * p.block_stride +
+                            (static_cast<int64_t>((n_ctx - 1) % kBlockTokens) * Hkv + h) * kHeadDim + 4 * lane;
+        knew = __ldcg(reinterpret_cast<const uint2*>(static_cast<const T*>(p.k_cache) + off));
+        vnew = __ldcg(reinterpret_cast<const uint2*>(static_cast<const T*>(p.v_cache) + off));
+      }
+    } else if (last) {
       const uint32_t* kn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(p.k_new) +
                                                              static_cast<int64_t>(b) * p.k_new_stride +
                                                              static_cast<int64_t>(h) * kHeadDim) + 2 * lane;
@@ -1086,8 +1113,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
           for (int i = 0; i < kStages; ++i)
             if (i == static_cast<int>(st)) blk = sblk[i];
           const int t = (n_ctx - 1) % kBlockTokens;
-          if (static_cast<unsigned long long>(static_cast<long long>(blk)) <
-              static_cast<unsigned long long>(p.num_blocks)) {
+          if (p.fuse_write && static_cast<unsigned long long>(static_cast<long long>(blk)) <
+                                  static_cast<unsigned long long>(p.num_blocks)) {
             const int64_t off = static_cast<int64_t>(blk) * p.block_stride +
                                 (static_cast<int64_t>(t) * Hkv + h) * kHeadDim + 4 * lane;
             *reinterpret_cast<uint2*>(static_cast<T*>(p.k_cache) + off) = knew;
@@ -1243,17 +1270,16 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   const int epoch = __shfl_sync(0xffffffffu, epoch_word, 0);
   const int stamp = static_cast<int>(static_cast<unsigned>(epoch) + 1u);  // this launch's flag value
 
-  // Publish this CTA's partials: the CTA's warps meet, then one thread stamps the CTA's flag
-  // with a release store. The barrier orders every thread's partial stores before that store,
-  // and a release is cumulative, so a reader that acquires the stamp sees all of them (no fence
-  // in every thread).
-  __syncthreads();
-  const int cta = static_cast<int>(blockIdx.x);
-  if (threadIdx.x == 0) st_release_gpu(&p.ws.cta_flag[cta * kFlagStride], stamp);
+  // Publish this warp's partials: the lanes meet, then lane 0 stamps the warp's flag with a
+  // release store. The warp barrier orders every lane's partial stores before that store, and a
+  // release is cumulative, so a reader that acquires the stamp sees all of them. Warps publish
+  // independently: a merge waits only for the warps that computed its pair's pieces.
+  __syncwarp();
+  if (lane == 0) st_release_gpu(&p.ws.warp_flag[gw * kFlagStride], stamp);
 
   // The split merge: the plan spreads the merge items evenly over all warps; an item waits
-  // only for the flags of the CTAs that computed its pair's pieces (lanes watch up to 32 of
-  // them at once). CTAs publish before they merge and all CTAs of the grid are resident
+  // only for the flags of the warps that computed its pair's pieces (lanes watch up to 32 of
+  // them at once). Warps publish before they merge and all CTAs of the grid are resident
   // together (one per SM), so the waits end; they are bounded all the same.
   int ready_entry = -1;  // entry whose producer CTAs are known to have published
   if (share_ok) {
@@ -1268,12 +1294,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         break;
       }
       if (ready_entry != entry) {
-        const int c0 = me.w & 0xffff, nc = me.w >> 16;
+        const int w0 = me.w & 0xffff, nw = me.w >> 16;
         int ok = 1;
-        for (int i = 0; i < nc && ok; i += 32) {
-          const int cc = c0 + i + lane;
+        for (int i = 0; i < nw && ok; i += 32) {
+          const int ww = w0 + i + lane;
           ok = __all_sync(0xffffffffu,
-                          i + lane >= nc || cc == cta || flag_wait(&p.ws.cta_flag[cc * kFlagStride], stamp));
+                          i + lane >= nw || ww == gw || flag_wait(&p.ws.warp_flag[ww * kFlagStride], stamp));
         }
         __syncwarp();  // orders the lanes' acquiring flag reads before every lane's partial loads
         if (!ok) {
@@ -1502,8 +1528,9 @@ int decode_prepare(DecodeLaunch* dl, void* out, int64_t out_stride, const void* 
   prm.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // log2(e)
   prm.q_bulk = (aligned(q, 16) && q_stride % 8 == 0) ? 1 : 0;
   prm.plan_ready = 0;
-  prm.prefetch_kv = (flags & AEG_DECODE_PREFETCH) ? 1 : 0;
+  prm.prefetch_kv = (flags & (AEG_DECODE_PREFETCH | AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE)) ? 1 : 0;
   prm.fuse_write = fuse ? 1 : 0;
+  prm.refresh_last = (!fuse && (flags & AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE) && !(flags & AEG_DECODE_PREFETCH)) ? 1 : 0;
   prm.k_new = k_new;
   prm.v_new = v_new;
   prm.k_new_stride = k_new_stride;

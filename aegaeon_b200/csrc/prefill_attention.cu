@@ -56,24 +56,31 @@ __device__ __forceinline__ float ex2p(float x) {
 // TMEM and returns without writing.
 constexpr int kTM = 128;                 // query rows per tile (two tiles per CTA)
 constexpr int kTN = 64;                  // keys per tile
-constexpr int kTStages = 3;
 constexpr int kTThreads = 9 * 32;        // 2 softmax warpgroups + the issuer warp
 constexpr int kQHalf = kTM * 128;        // one SW128 box of Q: 128 rows x 64 elements (16 KiB)
 constexpr int kKHalf = kTN * 128;        // one SW128 box of K or V: 64 rows x 64 elements (8 KiB)
-constexpr int kOffQ = 0;                                  // Q_A, Q_B: 2 halves each
-constexpr int kOffK = kOffQ + 4 * kQHalf;                 // stage s: 2 halves
-constexpr int kOffV = kOffK + kTStages * 2 * kKHalf;      // stage s: 2 halves
-constexpr int kOffP = kOffV + kTStages * 2 * kKHalf;      // P_A, P_B: 128 rows x 64 keys
-constexpr int kOffPl = kOffP + 2 * kQHalf;                // bf16 residues of P_A, P_B
-constexpr int kOffBar = kOffPl + 2 * kQHalf;
-constexpr int kTSmem = kOffBar + 256 + 1024;              // + 1024-byte alignment slack
-constexpr uint32_t kTmemCols = 512;                       // S_A[2], S_B[2] (64 each), O_A, O_B (128 each)
+constexpr uint32_t kTmemCols = 512;      // S_A[2], S_B[2] (64 each), O_A, O_B (128 each)
 constexpr uint64_t kTcWaitNs = 2000000000ull;
-constexpr float kRescaleAbove = 8.f;                      // exp2 domain
+constexpr float kRescaleAbove = 8.f;     // exp2 domain
 
-// mbarrier slots
-constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = 4, kBarKFree = 7, kBarVFree = 10, kBarSFull = 13,  // S: [X][buf]
-    kBarPFull = 17, kBarPv = 19, kBarDrain = 21, kBarCount = 22;
+// Shared-memory layout per element type: bf16 keeps a second P tile per query tile (the
+// rounding residue of P) and a 3-stage K/V ring; fp16 needs no residue and uses the room for a
+// 4-stage ring.
+template <bool kSplitP>
+struct TcLayout {
+  static constexpr int kStages = kSplitP ? 3 : 4;
+  static constexpr int kOffQ = 0;                                   // Q_A, Q_B: 2 halves each
+  static constexpr int kOffK = kOffQ + 4 * kQHalf;                  // stage s: 2 halves
+  static constexpr int kOffV = kOffK + kStages * 2 * kKHalf;        // stage s: 2 halves
+  static constexpr int kOffP = kOffV + kStages * 2 * kKHalf;        // P_A, P_B: 128 rows x 64 keys
+  static constexpr int kOffPl = kOffP + 2 * kQHalf;                 // bf16 residues of P_A, P_B
+  static constexpr int kOffBar = kOffPl + (kSplitP ? 2 * kQHalf : 0);
+  static constexpr int kSmem = kOffBar + 256 + 1024;                // + 1024-byte alignment slack
+};
+
+// mbarrier slots (K/V slots sized for up to 4 stages)
+constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = 5, kBarKFree = 9, kBarVFree = 13, kBarSFull = 17,  // S: [X][buf]
+    kBarPFull = 21, kBarPv = 23, kBarDrain = 25, kBarCount = 26;
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
@@ -146,6 +153,21 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+
+// The 64 fp32 columns of this thread's TMEM lane starting at `taddr`, in one round trip: the load
+// and its wait are one statement, so no use of the registers can be placed before the wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTThreads, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -153,14 +175,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                   const int32_t* __restrict__ cu_seqlens, int64_t num_tokens, int max_seqlen, int G,
                   float scale_log2) {
   constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  using LY = TcLayout<kSplitP>;
+  constexpr int kSt = LY::kStages;
   extern __shared__ uint8_t tsmem_raw[];
   const uint32_t raw = smem_u32(tsmem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* smem = tsmem_raw + (base - raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8 * kBarCount);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kOffBar + 8 * kBarCount + 4);  // the issuer gave up
-  auto bar_u32 = [&](int i) { return base + kOffBar + 8u * static_cast<uint32_t>(i); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::kOffBar + 8 * kBarCount);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + LY::kOffBar + 8 * kBarCount + 4);  // the issuer gave up
+  auto bar_u32 = [&](int i) { return base + LY::kOffBar + 8u * static_cast<uint32_t>(i); };
 
   const int tile_m = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // heaviest first
   const int h = blockIdx.y, b = blockIdx.z;
@@ -196,19 +220,23 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   const uint32_t tmem = *tmem_slot;
   auto tmem_s = [&](int x, int buf) { return tmem + static_cast<uint32_t>((x * 2 + buf) * 64); };
   auto tmem_o = [&](int x) { return tmem + 256u + static_cast<uint32_t>(x) * 128u; };
-  const uint32_t sQ = base + kOffQ;
+  const uint32_t sQ = base + LY::kOffQ;
   auto sQx = [&](int x) { return sQ + static_cast<uint32_t>(x) * 2 * kQHalf; };
-  auto sK = [&](int st) { return base + kOffK + static_cast<uint32_t>(st) * 2 * kKHalf; };
-  auto sV = [&](int st) { return base + kOffV + static_cast<uint32_t>(st) * 2 * kKHalf; };
-  auto sP = [&](int x) { return base + kOffP + static_cast<uint32_t>(x) * kQHalf; };
-  auto sPl = [&](int x) { return base + kOffPl + static_cast<uint32_t>(x) * kQHalf; };
+  auto sK = [&](int st) { return base + LY::kOffK + static_cast<uint32_t>(st) * 2 * kKHalf; };
+  auto sV = [&](int st) { return base + LY::kOffV + static_cast<uint32_t>(st) * 2 * kKHalf; };
+  auto sP = [&](int x) { return base + LY::kOffP + static_cast<uint32_t>(x) * kQHalf; };
+  auto sPl = [&](int x) { return base + LY::kOffPl + static_cast<uint32_t>(x) * kQHalf; };
 
   bool abort = false;
   if (warp == 8) {
     // ------------------------------- issuer -------------------------------
+    // Per key tile j, for query tile A then B: O_x += P_x V(j) as soon as softmax x has published
+    // P_x(j), then S_x(j + 1) right behind it, so that each warpgroup's next scores follow its own
+    // P V and do not wait for the other warpgroup's softmax. The tensor pipe completes a thread's
+    // MMAs in order, so S_x(j + 1) landing also means O_x += P_x V(j) is done.
     if ((tid & 31) == 0) {
       auto issue_kv = [&](int t) {
-        const int st = t % kTStages;
+        const int st = t % kSt;
         const int y = s0 + t * kTN, x = kvh * 128;
         mbar_arrive_expect_tx(&bars[kBarKFull + st], 2 * kKHalf);
         tma_load_2d(sK(st), &kmap, bar_u32(kBarKFull + st), x, y);
@@ -225,35 +253,42 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQ), h * 128 + 64, s0 + q0 + kTM);
       }
       int issued = 0;
-      for (; issued < min(kTStages, n_tiles); ++issued) issue_kv(issued);
+      for (; issued < min(kSt, n_tiles); ++issued) issue_kv(issued);
       const uint32_t id_s = idesc_f16<T>(kTN, false), id_o = idesc_f16<T>(128, true);
       bool ok = mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs);
-      int done_k = 0;  // key tiles whose K and V loads were seen landing
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kTStages;
-        const uint32_t ph = static_cast<uint32_t>((j / kTStages) & 1);
-        ok = mbar_wait_bounded(&bars[kBarKFull + st], ph, kTcWaitNs);
-        if (!ok) break;
-        tc_fence_after();
-        for (int x = 0; x < 2; ++x) {
-          if (j >= (x == 0 ? nA : nB)) continue;
-          // S_x[j & 1] last held S_x(j - 2), which softmax x finished reading before it published
-          // P_x(j - 2); this thread waited for that before issuing O_x += P_x V(j - 2).
+      int k_seen = 0, v_seen = 0;  // key tiles whose K / V loads were seen landing
+      auto wait_k = [&](int t) {
+        ok = ok && mbar_wait_bounded(&bars[kBarKFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
+        if (ok) k_seen = t + 1;
+      };
+      // S_x(t) into S_x[t & 1]. That buffer last held S_x(t - 2), which softmax x read before it
+      // published P_x(t - 1), which this thread waited for before issuing S_x(t).
+      auto issue_s = [&](int x, int t) {
+        const int st = t % kSt;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t qo = static_cast<uint32_t>(kk >> 2) * kQHalf + static_cast<uint32_t>(kk & 3) * 32;
-            const uint32_t ko = static_cast<uint32_t>(kk >> 2) * kKHalf + static_cast<uint32_t>(kk & 3) * 32;
-            umma_f16(tmem_s(x, j & 1), sw128_desc(sQx(x) + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
-                     kk > 0);
-          }
-          umma_commit(bar_u32(kBarSFull + x * 2 + (j & 1)));
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t qo = static_cast<uint32_t>(kk >> 2) * kQHalf + static_cast<uint32_t>(kk & 3) * 32;
+          const uint32_t ko = static_cast<uint32_t>(kk >> 2) * kKHalf + static_cast<uint32_t>(kk & 3) * 32;
+          umma_f16(tmem_s(x, t & 1), sw128_desc(sQx(x) + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
+                   kk > 0);
         }
-        if (!ok) break;
-        umma_commit(bar_u32(kBarKFree + st));
-        // refill the stage of tile j - 1 (its MMAs precede S(j) in the tensor pipe) with tile j + 2
+        umma_commit(bar_u32(kBarSFull + x * 2 + (t & 1)));
+      };
+      if (n_tiles > 0) {
+        wait_k(0);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          if (nB > 0) issue_s(1, 0);
+        }
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kSt;
+        const uint32_t ph = static_cast<uint32_t>((j / kSt) & 1);
+        // refill the stage of tile j - 1 (all its readers were issued by the end of iteration j - 1)
         if (j >= 1 && issued < n_tiles) {
-          const int ps = (j - 1) % kTStages;
-          const uint32_t pph = static_cast<uint32_t>(((j - 1) / kTStages) & 1);
+          const int ps = (j - 1) % kSt;
+          const uint32_t pph = static_cast<uint32_t>(((j - 1) / kSt) & 1);
           ok = mbar_wait_bounded(&bars[kBarKFree + ps], pph, kTcWaitNs) &&
                mbar_wait_bounded(&bars[kBarVFree + ps], pph, kTcWaitNs);
           if (!ok) break;
@@ -261,9 +296,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
         ok = mbar_wait_bounded(&bars[kBarVFull + st], ph, kTcWaitNs);
         if (!ok) break;
-        done_k = j + 1;
+        v_seen = j + 1;
+        if (j + 1 < n_tiles) {
+          wait_k(j + 1);
+          if (!ok) break;
+        }
+        tc_fence_after();
         for (int x = 0; x < 2; ++x) {
-          if (j >= (x == 0 ? nA : nB)) continue;
+          const int nx = x == 0 ? nA : nB;
+          if (j >= nx) continue;
           ok = mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
           if (!ok) break;
           tc_fence_after();
@@ -276,15 +317,17 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                        id_o, 1u);
           }
           umma_commit(bar_u32(kBarPv + x));
+          if (j + 1 < nx) issue_s(x, j + 1);
         }
         if (!ok) break;
+        umma_commit(bar_u32(kBarKFree + st));  // K(j) was read by S(j), issued before this point
         umma_commit(bar_u32(kBarVFree + st));
       }
       if (ok && n_tiles > 0) {  // the last tile's release commits have landed before the CTA exits
         const int t = n_tiles - 1;
-        const uint32_t tph = static_cast<uint32_t>((t / kTStages) & 1);
-        ok = mbar_wait_bounded(&bars[kBarKFree + t % kTStages], tph, kTcWaitNs) &&
-             mbar_wait_bounded(&bars[kBarVFree + t % kTStages], tph, kTcWaitNs);
+        const uint32_t tph = static_cast<uint32_t>((t / kSt) & 1);
+        ok = mbar_wait_bounded(&bars[kBarKFree + t % kSt], tph, kTcWaitNs) &&
+             mbar_wait_bounded(&bars[kBarVFree + t % kSt], tph, kTcWaitNs);
       }
       // every MMA this thread issued has completed before TMEM is freed
       umma_commit(bar_u32(kBarDrain));
@@ -294,11 +337,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         __threadfence_block();
         atomicOr(&g_deverr_prefill, AEG_DEVERR_WAIT_TIMEOUT);
         // loads issued but not seen landing: wait (bounded) before the CTA can exit
-        for (int t = done_k; t < issued; ++t) {
-          const uint32_t tph = static_cast<uint32_t>((t / kTStages) & 1);
-          mbar_wait_bounded(&bars[kBarKFull + t % kTStages], tph, kTcWaitNs);
-          mbar_wait_bounded(&bars[kBarVFull + t % kTStages], tph, kTcWaitNs);
-        }
+        for (int t = k_seen; t < issued; ++t)
+          mbar_wait_bounded(&bars[kBarKFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
+        for (int t = v_seen; t < issued; ++t)
+          mbar_wait_bounded(&bars[kBarVFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
         // release the softmax warpgroups from any wait on this thread
         for (int i = kBarSFull; i < kBarDrain; ++i) mbar_arrive(&bars[i]);
       }
@@ -322,20 +364,27 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         break;
       }
       tc_fence_after();
+      // The row's 64 scores in one TMEM round trip. Keys this row cannot see become -inf; a key
+      // tile that every row of the query tile sees whole (uniform over the warpgroup) needs no
+      // mask. The scale is positive, so the row maximum is taken on the raw scores and scaled
+      // once, and each exponent below is one fused multiply-add.
       const int key0 = j * kTN;
-      const uint32_t ts = tmem_s(x, j & 1) + lane_off;
+      float sv[64];
+      tmem_ld64(tmem_s(x, j & 1) + lane_off, sv);
       float mx = -INFINITY;
+      if (key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[16];
-        tmem_ld16(ts + c * 16, v);
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int key = key0 + c * 16 + i;
-          mx = fmaxf(mx, (key <= row && key < L) ? v[i] * scale_log2 : -INFINITY);
+        for (int i = 0; i < 64; ++i) {
+          const int key = key0 + i;
+          sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
+          mx = fmaxf(mx, sv[i]);
         }
       }
-      // P_x is free once O_x += P_x V(j - 1) has completed; O_x may be rescaled from then on
+      mx *= scale_log2;
+      // P_x is free and O_x stable once O_x += P_x V(j - 1) has completed (it precedes S_x(j))
       if (j > 0) {
         bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
         if (group_any(1 + x, bad)) {
@@ -363,18 +412,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         l *= factor;
         m_used = mx;
       }
-      const float base_m = m_used == -INFINITY ? 0.f : m_used;
+      const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
       float rs = 0.f;
+      const uint32_t roff = static_cast<uint32_t>(r) * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float v[16];
-        tmem_ld16(ts + c * 16, v);
         uint32_t pk[8], pr[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          const int key = key0 + c * 16 + i;
-          const float p0 = (key <= row && key < L) ? ex2p(v[i] * scale_log2 - base_m) : 0.f;
-          const float p1 = (key + 1 <= row && key + 1 < L) ? ex2p(v[i + 1] * scale_log2 - base_m) : 0.f;
+          const float p0 = ex2p(fmaf(sv[c * 16 + i], scale_log2, neg_base));  // masked keys: ex2(-inf) = 0
+          const float p1 = ex2p(fmaf(sv[c * 16 + i + 1], scale_log2, neg_base));
           rs += p0 + p1;
           pk[i >> 1] = pack2<T>(p0, p1);
           if constexpr (kSplitP) {
@@ -383,7 +430,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           }
         }
         // keys c*16 .. c*16+15 of row r: 16-byte chunks 2c and 2c + 1 of the row, swizzled
-        const uint32_t roff = static_cast<uint32_t>(r) * 128;
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
           const uint32_t chunk = (static_cast<uint32_t>(c * 2 + q2) ^ static_cast<uint32_t>(r & 7)) * 16;
@@ -487,13 +533,14 @@ int launch_prefill_tc(void* out, int64_t o_stride, const void* q, int64_t q_stri
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!configured[dev]) {
-      AEG_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmem));
+      AEG_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TcLayout<std::is_same<T, __nv_bfloat16>::value>::kSmem));
       configured[dev] = true;
     }
   }
   const dim3 grid(static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)), static_cast<unsigned>(Hq),
                   static_cast<unsigned>(B));
-  prefill_tc_kernel<T><<<grid, kTThreads, kTSmem, stream>>>(
+  prefill_tc_kernel<T><<<grid, kTThreads, TcLayout<std::is_same<T, __nv_bfloat16>::value>::kSmem, stream>>>(
       qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, max_seqlen, Hq / Hkv,
       static_cast<float>(static_cast<double>(scale) * 1.4426950408889634));
   AEG_CHECK_LAUNCH("prefill_attention(tcgen05)");

@@ -21,7 +21,7 @@ import numpy as np
 import torch
 
 from . import _native
-from ._native import AEG_DECODE_PREFETCH, check, lib
+from ._native import AEG_DECODE_PREFETCH, AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE, check, lib
 from .layout import BLOCK_SIZE, block_bytes
 
 _DTYPES = {torch.float16: _native.AEG_DTYPE_FP16, torch.bfloat16: _native.AEG_DTYPE_BF16}
@@ -563,7 +563,7 @@ class DecodePlan:
 def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                       block_table: torch.Tensor, cache_seqlens: torch.Tensor, softmax_scale: float | None = None,
                       out: torch.Tensor | None = None, plan: DecodePlan | None = None,
-                      prefetch: bool = False) -> torch.Tensor:
+                      prefetch: bool = False, after_decode_write: bool = False) -> torch.Tensor:
     """Paged decode attention with one query token per sequence (vLLM FlashAttention decode call).
 
     query ``[B, Hq, D]``; key_cache/value_cache ``(N, 16, Hkv, D)`` views (any block stride);
@@ -571,6 +571,10 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
     ``plan`` must have been built for these ``cache_seqlens`` and ``W``; without one a plan is built
     on the fly (an extra launch). ``prefetch=True`` promises that the kernel launched just before
     on this stream writes neither these cache blocks nor the block table (``AEG_DECODE_PREFETCH``).
+    ``after_decode_write=True`` promises that it wrote at most each sequence's newest position
+    ``cache_seqlens[b] - 1`` (the decode ``reshape_and_cache_flash``) and no block table
+    (``AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE``): tiles are requested early and that row is read
+    again after the preceding kernel has finished.
     """
     _require_cuda(query, "query")
     if query.dim() != 3 or query.stride(2) != 1 or query.stride(1) != query.size(2):
@@ -617,7 +621,9 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
                                        key_cache.size(0), block_table.data_ptr(), block_table.stride(0),
                                        cache_seqlens.data_ptr(), B, Hq, Hkv, D, scale, _DTYPES[query.dtype],
                                        plan.workspace.data_ptr(), plan.workspace.numel(),
-                                       AEG_DECODE_PREFETCH if prefetch else 0, _stream(dev))
+                                       (AEG_DECODE_PREFETCH if prefetch else 0)
+                                       | (AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE if after_decode_write else 0),
+                                       _stream(dev))
     check(st, "paged_attention_decode")
     return out
 
@@ -692,7 +698,9 @@ def decode_layer(out: torch.Tensor, query: torch.Tensor, key: torch.Tensor, valu
 
 def paged_attention_decode(out: torch.Tensor, query: torch.Tensor, kv_cache: torch.Tensor, layer: int,
                            block_tables: torch.Tensor, seq_lens: torch.Tensor, scale: float,
-                           plan: DecodePlan | None = None, prefetch: bool = False) -> None:
+                           plan: DecodePlan | None = None, prefetch: bool = False,
+                           after_decode_write: bool = False) -> None:
     """Decode attention of ``layer`` over Aegaeon's ``(N, L, 2, 16, Hkv, D)`` cache, into ``out``."""
     kc, vc = _layer_views(kv_cache, layer)
-    flash_attn_decode(query, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan, prefetch=prefetch)
+    flash_attn_decode(query, kc, vc, block_tables, seq_lens, scale, out=out, plan=plan, prefetch=prefetch,
+                      after_decode_write=after_decode_write)

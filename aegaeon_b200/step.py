@@ -69,9 +69,12 @@ class DecodeStep:
                 ops.decode_layer(self.out[layer], self.q[layer], self.k_new[layer], self.v_new[layer], self.kv_cache,
                                  layer, self.block_tables, self.seq_lens, self.scale, plan=self.plan, prefetch=True)
             else:
+                # The cache write stores each sequence's newest row (slot_mapping holds the decode
+                # slots, position seq_len - 1): the attention may request its tiles early and
+                # reads that row again once the write has finished.
                 ops.reshape_and_cache(self.k_new[layer], self.v_new[layer], self.kv_cache, layer, self.slot_mapping)
                 ops.paged_attention_decode(self.out[layer], self.q[layer], self.kv_cache, layer, self.block_tables,
-                                           self.seq_lens, self.scale, plan=self.plan)
+                                           self.seq_lens, self.scale, plan=self.plan, after_decode_write=True)
 
     def capture(self) -> "DecodeStep":
         """Records one step into a CUDA graph (after one eager warm-up step on a side stream)."""

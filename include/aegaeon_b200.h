@@ -273,10 +273,10 @@ AEG_API int aeg_reshape_and_cache(const void* key, const void* value, int64_t ke
  * the per-step attention metadata at worker.py:694-711) and then aeg_paged_attn_decode (or
  * aeg_decode_layer) once per layer with the same workspace. The workspace is caller-owned device
  * memory of at least aeg_decode_workspace_size(B, Hq, Hkv, D) bytes, 256-byte aligned, used by
- * one stream at a time. The plan cuts every (sequence, KV head) into block ranges of near-equal
- * length (longest first), which the warps of a persistent kernel take from an atomic counter;
- * ranges of a split (sequence, head) are merged at the end of the same launch, each merge
- * waiting only for the CTAs that computed its pieces.
+ * one stream at a time. The plan cuts the batch's (block, KV head) items, in
+ * (sequence, head) order, into one contiguous range of equal cost per worker warp of the
+ * attention grid (8 warps x one CTA per SM); a (sequence, head) cut across warps is merged at
+ * the end of the same launch, each merge waiting only for the warps that computed its pieces.
  *
  * Supported: D = 128; Hq % Hkv == 0; Hq / Hkv <= 16; fp16 or bf16; 16-byte aligned K/V
  * bases; a block stride that is a multiple of 8 elements; q/out with even token strides.
@@ -292,8 +292,14 @@ AEG_API int aeg_decode_plan(void* workspace, size_t workspace_bytes, const int32
  * `stream`, so the launch may request its first K/V tiles before that kernel has finished (the
  * query rows and new K/V rows are still read only after it). Safe between consecutive layers of
  * one decode step (a layer writes only its own layer's rows); not after a cache write, a block
- * copy or a swap of the same layer. */
+ * copy or a swap of the same layer.
+ * AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE (aeg_paged_attn_decode): the kernel that immediately
+ * precedes the call wrote, of what the call reads, at most position seq_lens[b] - 1 of each
+ * sequence (the decode cache write of aeg_reshape_and_cache with the slots the reference builds
+ * for a decode step) and no block table. The launch requests its first tiles early and reads
+ * each sequence's newest row again after that kernel has finished. */
 #define AEG_DECODE_PREFETCH 0x1
+#define AEG_DECODE_PREFETCH_AFTER_DECODE_WRITE 0x2
 
 AEG_API int aeg_paged_attn_decode(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                           const void* k_cache, const void* v_cache, int64_t block_stride,

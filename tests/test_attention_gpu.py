@@ -173,6 +173,40 @@ def test_fused_decode_layer_equals_write_then_attend(cuda_device, dtype, Hq, Hkv
     assert_attention_close(out_b, want, f"fused Hq={Hq} Hkv={Hkv} {dtype}")
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (16, 1)])
+def test_attention_after_decode_write_requests_tiles_early(cuda_device, dtype, Hq, Hkv):
+    # reshape_and_cache at the decode slots, then paged_attention_decode launched right behind it
+    # with after_decode_write=True: the attention requests its first tiles before the write has
+    # finished and reads each sequence's newest row again afterwards. Two rounds with different
+    # new rows, each equal bit for bit to the fused layer on a separate copy of the cache.
+    seq_lens = [1, 15, 16, 17, 300, 2500, 64, 33, 4000, 2]
+    B = len(seq_lens)
+    kv, q, tables, sl = decode_case(B, Hq, Hkv, seq_lens, dtype, num_layers=2, seed=Hq * 7 + Hkv)
+    t = torch.as_tensor(tables, device=cuda_device)
+    s = torch.as_tensor(sl, device=cuda_device)
+    pos = sl.astype(np.int64) - 1
+    slots = torch.as_tensor(tables[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16, device=cuda_device)
+    layer = 1
+    kv_c = kv.clone()
+    plan = ops.DecodePlan(B, Hq, Hkv, 128, cuda_device).plan(s, t)
+    ops.paged_attention_decode(torch.empty_like(q), q, kv_c, 0, t, s, SCALE, plan=plan)  # the plan is now complete
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    for rnd in range(2):
+        k_new = torch.randn((B, Hkv, 128), generator=g, device=cuda_device).to(dtype)
+        v_new = torch.randn((B, Hkv, 128), generator=g, device=cuda_device).to(dtype)
+        out_c = torch.full_like(q, float("nan"))
+        ops.reshape_and_cache(k_new, v_new, kv_c, layer, slots)
+        ops.paged_attention_decode(out_c, q, kv_c, layer, t, s, SCALE, plan=plan, after_decode_write=True)
+        kv_b = kv.clone()
+        out_b = torch.full_like(q, float("nan"))
+        ops.decode_layer(out_b, q, k_new, v_new, kv_b, layer, t, s, SCALE)
+        torch.cuda.synchronize()
+        assert torch.equal(kv_c[:, layer].view(torch.int16), kv_b[:, layer].view(torch.int16))
+        assert torch.equal(out_c.view(torch.int16), out_b.view(torch.int16)), f"round {rnd}"
+    assert ops.read_device_errors() == 0
+
+
 @pytest.mark.parametrize("name", ["vllm_cfg1_fp16.npz", "vllm_gqa8_bf16.npz"])
 def test_matches_vllm_golden_vectors(cuda_device, name):
     # Same inputs as vLLM's kernels in tests/golden/make_golden.py: the cache write of the
