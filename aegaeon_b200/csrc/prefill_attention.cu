@@ -117,7 +117,6 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
 // OR of `v` over the 128 threads of named barrier `id` (a barrier itself: every thread must come).
 __device__ __forceinline__ bool group_any(int id, bool v) {
   uint32_t r;
@@ -186,12 +185,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + LY::kOffBar + 8 * kBarCount + 4);  // the issuer gave up
   auto bar_u32 = [&](int i) { return base + LY::kOffBar + 8u * static_cast<uint32_t>(i); };
 
-  const int tile_m = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // heaviest first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Blocks start in linear order (x fastest): the query-tile level is the outermost dimension,
+  // heaviest (last) tiles first over every prompt and head, so the lightest CTAs fill the tail.
+  const int tile_m = static_cast<int>(gridDim.z) - 1 - static_cast<int>(blockIdx.z);
+  const int h = blockIdx.x, b = blockIdx.y;
   const int s0 = cu_seqlens[b];
   const int L = cu_seqlens[b + 1] - s0;
   if (s0 < 0 || L < 0 || static_cast<int64_t>(s0) + L > num_tokens || L > max_seqlen) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && h == 0) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
+    if (threadIdx.x == 0 && blockIdx.z == 0 && h == 0) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
     return;
   }
   const int q0 = tile_m * 2 * kTM;
@@ -230,10 +231,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   bool abort = false;
   if (warp == 8) {
     // ------------------------------- issuer -------------------------------
-    // Per key tile j, for query tile A then B: O_x += P_x V(j) as soon as softmax x has published
-    // P_x(j), then S_x(j + 1) right behind it, so that each warpgroup's next scores follow its own
-    // P V and do not wait for the other warpgroup's softmax. The tensor pipe completes a thread's
-    // MMAs in order, so S_x(j + 1) landing also means O_x += P_x V(j) is done.
+    // Per key tile j, for query tile A then B: as soon as softmax x has published P_x(j), the
+    // scores S_x(j + 1) and then O_x += P_x V(j), so that each warpgroup's next scores follow its
+    // own softmax and do not wait for the other warpgroup's.
     if ((tid & 31) == 0) {
       auto issue_kv = [&](int t) {
         const int st = t % kSt;
@@ -308,6 +308,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           ok = mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
           if (!ok) break;
           tc_fence_after();
+          // S_x(j + 1) ahead of O_x += P_x V(j): softmax x computes its next maximum while the
+          // P V MMAs run, and waits for them only before it rescales O_x and rewrites P_x.
+          if (j + 1 < nx) issue_s(x, j + 1);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             umma_f16(tmem_o(x), sw128_desc(sP(x) + kk * 32, 16, 1024), sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
@@ -317,7 +320,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                        id_o, 1u);
           }
           umma_commit(bar_u32(kBarPv + x));
-          if (j + 1 < nx) issue_s(x, j + 1);
         }
         if (!ok) break;
         umma_commit(bar_u32(kBarKFree + st));  // K(j) was read by S(j), issued before this point
@@ -354,43 +356,52 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int nx = x == 0 ? nA : nB;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     float m_used = -INFINITY, l = 0.f;
-    // tcgen05.ld / st are warp-collective (.sync.aligned): every lane of a warp executes each of them,
-    // and each wait's outcome is made uniform over the warpgroup before anyone acts on it.
+    // tcgen05.ld / st are warp-collective (.sync.aligned): a wait's outcome is made uniform over
+    // the warp before the warp acts on it. The warpgroup meets once per key tile, at the barrier
+    // that publishes P, which also votes on a timeout: a warp whose wait gave up skips its work
+    // but still reaches that barrier, and then all four warps stop together.
+    bool bad = false;
     for (int j = 0; j < nx; ++j) {
-      bool bad = !mbar_wait_bounded(&bars[kBarSFull + x * 2 + (j & 1)], static_cast<uint32_t>((j >> 1) & 1), kTcWaitNs) ||
-                 *s_abort;
-      if (group_any(1 + x, bad)) {
-        abort = true;
-        break;
-      }
-      tc_fence_after();
+      bad = bad || *s_abort ||
+            !mbar_wait_bounded(&bars[kBarSFull + x * 2 + (j & 1)], static_cast<uint32_t>((j >> 1) & 1), kTcWaitNs);
+      bad = __any_sync(0xffffffffu, bad);
       // The row's 64 scores in one TMEM round trip. Keys this row cannot see become -inf; a key
       // tile that every row of the query tile sees whole (uniform over the warpgroup) needs no
       // mask. The scale is positive, so the row maximum is taken on the raw scores and scaled
       // once, and each exponent below is one fused multiply-add.
       const int key0 = j * kTN;
       float sv[64];
-      tmem_ld64(tmem_s(x, j & 1) + lane_off, sv);
       float mx = -INFINITY;
-      if (key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L) {
+      if (!bad) {
+        tc_fence_after();
+        tmem_ld64(tmem_s(x, j & 1) + lane_off, sv);
+        if (!(key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L)) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int key = key0 + i;
-          sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
-          mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < 64; ++i) {
+            const int key = key0 + i;
+            sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
+          }
         }
+        // eight independent partial maxima instead of one 64-long dependent chain
+        float mp[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mp[k] = sv[k];
+#pragma unroll
+        for (int i = 8; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
+        mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+        mx *= scale_log2;
       }
-      mx *= scale_log2;
-      // P_x is free and O_x stable once O_x += P_x V(j - 1) has completed (it precedes S_x(j))
-      if (j > 0) {
+      // P_x is free and O_x stable once O_x += P_x V(j - 1) has completed
+      if (j > 0 && !bad) {
         bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
-        if (group_any(1 + x, bad)) {
+        bad = __any_sync(0xffffffffu, bad);
+      }
+      if (bad) {  // this warp stops working; it still meets the others below
+        if (group_any(1 + x, true)) {
           abort = true;
           break;
         }
+        continue;
       }
       tc_fence_after();
       const bool grow = mx > m_used + kRescaleAbove;
@@ -413,7 +424,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         m_used = mx;
       }
       const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-      float rs = 0.f;
+      float rsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
       const uint32_t roff = static_cast<uint32_t>(r) * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -422,7 +433,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         for (int i = 0; i < 16; i += 2) {
           const float p0 = ex2p(fmaf(sv[c * 16 + i], scale_log2, neg_base));  // masked keys: ex2(-inf) = 0
           const float p1 = ex2p(fmaf(sv[c * 16 + i + 1], scale_log2, neg_base));
-          rs += p0 + p1;
+          rsum[(i >> 1) & 3] += p0 + p1;
           pk[i >> 1] = pack2<T>(p0, p1);
           if constexpr (kSplitP) {
             const float2 rr = unpack2<T>(pk[i >> 1]);
@@ -442,10 +453,13 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                          : "memory");
         }
       }
-      l += rs;
+      l += (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
       fence_async_smem();
       tc_fence_before();
-      group_sync(1 + x);
+      if (group_any(1 + x, false)) {  // P published by all four warps, unless one of them gave up
+        abort = true;
+        break;
+      }
       if (r == 0) mbar_arrive(&bars[kBarPFull + x]);
     }
     if (!abort && nx > 0) {
@@ -538,8 +552,8 @@ int launch_prefill_tc(void* out, int64_t o_stride, const void* q, int64_t q_stri
       configured[dev] = true;
     }
   }
-  const dim3 grid(static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)), static_cast<unsigned>(Hq),
-                  static_cast<unsigned>(B));
+  const dim3 grid(static_cast<unsigned>(Hq), static_cast<unsigned>(B),
+                  static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)));
   prefill_tc_kernel<T><<<grid, kTThreads, TcLayout<std::is_same<T, __nv_bfloat16>::value>::kSmem, stream>>>(
       qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, max_seqlen, Hq / Hkv,
       static_cast<float>(static_cast<double>(scale) * 1.4426950408889634));
@@ -578,7 +592,7 @@ int aeg_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t 
   AEG_CHECK_ARG(aeg::aligned(q, 16) && aeg::aligned(k, 16) && aeg::aligned(v, 16) && aeg::aligned(out, 4) &&
                     q_stride % 8 == 0 && k_stride % 8 == 0 && v_stride % 8 == 0 && out_stride % 2 == 0,
                 "prefill_attention: q/k/v must be 16-byte aligned with token strides that are multiples of 8 elements");
-  AEG_CHECK_ARG(max_seqlen <= (1 << 24) && B <= 65535 && Hq <= 65535, "prefill_attention: grid too large");
+  AEG_CHECK_ARG(max_seqlen <= 65535 * 256 && B <= 65535 && Hq <= 65535, "prefill_attention: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   AEG_CHECK_ARG(aeg::aligned(out, 16) && out_stride % 8 == 0,
                 "prefill_attention: out must be 16-byte aligned with a token stride that is a multiple of 8");
