@@ -655,7 +655,8 @@ def run_decode(args, world, rank, local):
     e1.record(stream)
     torch.cuda.synchronize(device)
     _barrier(world)
-    ms = _max_over_ranks(e0.elapsed_time(e1), world, device)
+    own_ms = e0.elapsed_time(e1)  # this rank's timed region
+    ms = _max_over_ranks(own_ms, world, device)
     clock_info = clocks.stop()
     assert torch.isfinite(step.out.float()).all(), "non-finite attention output"
 
@@ -762,15 +763,18 @@ def run_decode(args, world, rank, local):
     ms_step = ms / args.steps
     tokens_total = B * world if scaling == "weak" else cfg.batch
     value = tokens_total / (ms_step / 1e3)
-    # Per-rank figures of the dominant kernel, gathered; the line reports the slowest rank's.
-    in_step_ms = max((ms_step - plan_med_ms) / L, 1e-6)
+    # Per-rank figures of the dominant kernel from each rank's own timed step, gathered; the
+    # roofline reports the rank whose step bounds the job (the longest one).
+    own_step = own_ms / args.steps
+    in_step_ms = max((own_step - plan_med_ms) / L, 1e-6)
     if not step.fused:
-        in_step_ms = max((ms_step - plan_med_ms - L * write_graph_ms) / L, 1e-6)
+        in_step_ms = max((own_step - plan_med_ms - L * write_graph_ms) / L, 1e-6)
     attn_avg_ms = statistics.mean(attn_ms)
     per_rank = _gather_floats([launch_bytes, in_step_ms, attn_avg_ms, in_model_ms, algo["kv_read"] * L,
-                               (algo["attention"] + algo["reshape_and_cache"]) * L], world, device)
-    worst = min(range(world), key=lambda r: per_rank[r][0] / per_rank[r][1])
-    lb, ism, iso, imd = per_rank[worst][0], per_rank[worst][1], per_rank[worst][2], per_rank[worst][3]
+                               (algo["attention"] + algo["reshape_and_cache"]) * L, own_step], world, device)
+    bound = max(range(world), key=lambda r: per_rank[r][6])
+    lb, ism, iso, imd = per_rank[bound][0], per_rank[bound][1], per_rank[bound][2], per_rank[bound][3]
+    rank_bytes = [r[0] for r in per_rank]
     kv_step_all = sum(r[4] for r in per_rank)
     bytes_step_all = sum(r[5] for r in per_rank)
     achieved = lb / (ism / 1e3) / 1e9
@@ -793,7 +797,11 @@ def run_decode(args, world, rank, local):
         "data": "synthetic: seeded contexts, block tables and N(0, std^2) K/V/q (no dataset on this path)",
         "config": decode_config(cfg, world, fused=step.fused),
         "shard": {"rank0_batch": B, "rank0_pool_blocks": lay.num_blocks, "rank0_sum_ctx": lay.total_tokens,
-                  "rank0_layer_bytes": launch_bytes},
+                  "rank0_layer_bytes": launch_bytes,
+                  "layer_bytes_per_rank": rank_bytes,
+                  "imbalance": max(rank_bytes) / (sum(rank_bytes) / world),
+                  "in_step_frac_per_rank": [r[0] / (r[1] / 1e3) / 1e9 / peak for r in per_rank],
+                  "bound_rank": bound},
         "kv_read_gbs": kv_step_all / (ms_step / 1e3) / 1e9,
         "hbm_frac_step": bytes_step_all / world / (ms_step / 1e3) / 1e9 / peak,
         "e2e": {
@@ -818,7 +826,8 @@ def run_decode(args, world, rank, local):
             "peak_source": peak_src,
             "traffic": traffic,
             "algorithmic_bytes_per_launch": lb,
-            "duration": "per layer launch in the timed step graph: (step - plan) / layers, slowest rank",
+            "duration": "per layer launch in the timed step graph of the rank whose step bounds the job: "
+                        "(its step - plan) / layers",
             "in_step_launch_us": ism * 1e3,
             "avg_launch_us": iso * 1e3,
             "frac_isolated_launch": lb / (iso / 1e3) / 1e9 / peak,
