@@ -97,11 +97,30 @@ class DecodeLayout:
         return int(((self.seq_lens.astype(np.int64) + BLOCK_SIZE - 1) // BLOCK_SIZE).sum())
 
 
-def make_layout(cfg: DecodeConfig, rank: int = 0, world: int = 1) -> DecodeLayout:
-    """Seeded contexts and block assignment; with ``world > 1`` returns sequences i = rank mod world."""
+def balanced_split(ctx: np.ndarray, world: int) -> list[np.ndarray]:
+    """Sequence ids per rank with about equal total context: longest first, each to the rank with
+    the least context so far (lowest rank on ties); ids ascending within a rank."""
+    load = np.zeros(world, np.int64)
+    owner = np.empty(len(ctx), np.int64)
+    for i in sorted(range(len(ctx)), key=lambda i: (-int(ctx[i]), i)):
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += int(ctx[i])
+    return [np.flatnonzero(owner == r) for r in range(world)]
+
+
+def make_layout(cfg: DecodeConfig, rank: int = 0, world: int = 1, split: str = "mod") -> DecodeLayout:
+    """Seeded contexts and block assignment. With ``world > 1`` returns this rank's sequences:
+    ``split="mod"`` takes sequences i = rank mod world (equal counts), ``split="balanced"`` the
+    ranks' shares of ``balanced_split`` (about equal context)."""
     gen = torch.Generator().manual_seed(cfg.seed)
     ctx = draw_contexts(cfg, gen).numpy()
-    ids = np.arange(cfg.batch)[rank::world]
+    if split == "mod":
+        ids = np.arange(cfg.batch)[rank::world]
+    elif split == "balanced":
+        ids = balanced_split(ctx, world)[rank]
+    else:
+        raise ValueError(f"split must be 'mod' or 'balanced', not {split!r}")
     ctx = ctx[ids]
     nblk = (ctx + BLOCK_SIZE - 1) // BLOCK_SIZE
     need = int(nblk.sum())

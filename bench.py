@@ -56,6 +56,8 @@ def _args():
     p.add_argument("--swap-scale", type=float, default=1.0, help="decode configs: scale the swap set (small cases)")
     p.add_argument("--unfused", action="store_true",
                    help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
+    p.add_argument("--split", choices=["mod", "balanced"], default="mod",
+                   help="cfg3 under torchrun: sequence i on rank i mod N (default), or shares of about equal context")
     p.add_argument("--layers", type=int, default=0,
                    help="decode configs, profiling only: override the layer count (same work per launch, smaller pool)")
     p.add_argument("--compact-pool", action="store_true",
@@ -159,13 +161,14 @@ class ClockSampler:
 # The workload description shared by both arms (the reference arm prints the same dict)
 
 
-def _decode_layout(cfg, world: int, rank: int):
-    """This rank's share of a decode config: cfg3 splits its batch i mod N over the ranks (strong
-    scaling, the split BASELINE.json names); the others run the whole batch on every rank."""
+def _decode_layout(cfg, world: int, rank: int, split: str = "mod"):
+    """This rank's share of a decode config: cfg3 splits its batch over the ranks (strong scaling;
+    by default sequence i on rank i mod N, the split BASELINE.json names); the others run the
+    whole batch on every rank."""
     from aegaeon_b200 import synth
 
     if cfg.name == "cfg3":
-        return synth.make_layout(cfg, rank, world), "strong"
+        return synth.make_layout(cfg, rank, world, split), "strong"
     return synth.make_layout(cfg), "weak"
 
 
@@ -176,7 +179,7 @@ def _ctx_desc(cfg) -> str:
     return f"round(lognormal({d[1]}, {d[2]})) clipped to [{d[3]}, {d[4]}]"
 
 
-def decode_config(cfg, world: int, fused: bool = True) -> dict:
+def decode_config(cfg, world: int, fused: bool = True, split: str = "mod") -> dict:
     """The ``config`` object of a decode line, identical in both arms (whole job at ``world`` GPUs)."""
     from aegaeon_b200 import synth
 
@@ -186,13 +189,16 @@ def decode_config(cfg, world: int, fused: bool = True) -> dict:
     batch = cfg.batch if strong else cfg.batch * world
     sum_ctx = full.total_tokens * (1 if strong else world)
     kv_step = sum_ctx * Hkv * D * 2 * 2 * L
-    if strong:
-        split = f"batch {cfg.batch} split over {world} GPU(s): sequence i on GPU i mod {world}, each GPU its own pool"
+    if strong and split == "balanced":
+        how = (f"batch {cfg.batch} split over {world} GPU(s) in shares of about equal context (longest first to "
+               "the least-loaded GPU), each GPU its own pool")
+    elif strong:
+        how = f"batch {cfg.batch} split over {world} GPU(s): sequence i on GPU i mod {world}, each GPU its own pool"
     else:
-        split = f"batch {cfg.batch} per GPU on each of {world} GPU(s), each GPU its own pool"
+        how = f"batch {cfg.batch} per GPU on each of {world} GPU(s), each GPU its own pool"
     return {
         "workload": f"{cfg.name}: {cfg.model} decode step, {L} layers x (reshape_and_cache of one new token per "
-                    f"sequence + paged decode attention), {split}",
+                    f"sequence + paged decode attention), {how}",
         "batch": batch, "layers": L, "q_heads": Hq, "kv_heads": Hkv, "head_dim": D, "block_size": 16,
         "storage_dtype": "bf16" if cfg.dtype == torch.bfloat16 else "fp16",
         "context_lengths": _ctx_desc(cfg), "seed": cfg.seed, "value_std": cfg.value_std,
@@ -600,7 +606,7 @@ def run_decode(args, world, rank, local):
     cfg = synth.CONFIGS[args.config]
     if args.layers:
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
-    lay, scaling = _decode_layout(cfg, world, rank)
+    lay, scaling = _decode_layout(cfg, world, rank, args.split)
     if args.compact_pool:
         lay = synth.compact_layout(lay)
     B = len(lay.seq_lens)
@@ -795,7 +801,7 @@ def run_decode(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "fp16" if cfg.dtype == torch.float16 else "bf16",
         "data": "synthetic: seeded contexts, block tables and N(0, std^2) K/V/q (no dataset on this path)",
-        "config": decode_config(cfg, world, fused=step.fused),
+        "config": decode_config(cfg, world, fused=step.fused, split=args.split),
         "shard": {"rank0_batch": B, "rank0_pool_blocks": lay.num_blocks, "rank0_sum_ctx": lay.total_tokens,
                   "rank0_layer_bytes": launch_bytes,
                   "layer_bytes_per_rank": rank_bytes,
@@ -1331,7 +1337,7 @@ def run_reference(args, world, rank):
         "scaling": "strong" if cfg.name == "cfg3" else "weak", "vs_baseline": None,
         "dtype": "fp16" if cfg.dtype == torch.float16 else "bf16", "impl": "reference",
         "data": "synthetic: seeded contexts, block tables and N(0, std^2) K/V/q (no dataset on this path)",
-        "config": decode_config(cfg, world, fused=not args.unfused),
+        "config": decode_config(cfg, world, fused=not args.unfused, split=args.split),
         "compute": "fp32 (storage dtype in and out)",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": smp.threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -92,3 +92,19 @@ def test_weight_switch_workload_is_qwen2_7b():
     assert len(sizes) == 2 + 28 * 12 + 1           # embeddings, 12 tensors per layer, final norm, lm head
     assert sum(sizes) == 15_231_233_024             # 7.6B bf16 parameters
     assert sizes[0] == sizes[-1] == 152064 * 3584 * 2
+
+
+def test_balanced_split_assigns_every_sequence_once_with_even_context():
+    from aegaeon_b200 import synth
+
+    cfg = synth.CONFIGS["cfg3"]
+    for world in (1, 2, 4, 8):
+        lays = [synth.make_layout(cfg, r, world, "balanced") for r in range(world)]
+        ids = np.concatenate([l.seq_ids for l in lays])
+        assert sorted(ids.tolist()) == list(range(cfg.batch))
+        tot = [l.total_tokens for l in lays]
+        assert max(tot) - min(tot) <= int(synth.make_layout(cfg).seq_lens.max())  # within one sequence
+        for l in lays:  # each rank's pool holds exactly its own blocks
+            assert l.num_blocks == l.total_blocks
+    mod = [synth.make_layout(cfg, r, 8).seq_ids for r in range(8)]
+    assert [m.tolist() for m in mod] == [list(range(r, cfg.batch, 8)) for r in range(8)]
