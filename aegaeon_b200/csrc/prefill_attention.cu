@@ -13,9 +13,12 @@
 // last query tile of a prompt sees the most keys). Measured and rejected: an mma.sync kernel (64
 // rows per CTA, cp.async double buffering; fp16 206 / bf16 163 TFLOP/s on the bench prompts), a
 // serialized tcgen05 kernel (one 128-row tile, O folded into registers every key tile: 171 / 139),
-// issuing S(j + 1) ahead of O += P V(j) (the in-order tensor pipe then delays the P V the softmax
-// waits for: 0.356 vs 0.316 ms), and a mask-free softmax path for fully visible key tiles (a
-// branch around the warp-collective TMEM loads: 0.414 vs 0.316 ms).
+// a mask-free softmax path for fully visible key tiles (a branch around the warp-collective TMEM
+// loads: 0.414 vs 0.316 ms), one thread issuing every load and MMA with P through shared memory
+// (284 / 328: a refill waited for all MMAs of the previous key tile before the next P was
+// served), and one MMA thread serving both query tiles in the order their P arrive (312 / 360
+// with one thread vs 357 / 409 with one per query tile: issuing a tile's P V and next scores
+// takes that thread 0.5-0.6 us).
 #include "aeg_common.cuh"
 
 #include <cuda.h>
@@ -40,47 +43,50 @@ __device__ __forceinline__ float ex2p(float x) {
 // ---------------------------------------------------------------------------------------
 // tcgen05 kernel. One CTA = 256 query rows of one head of one prompt as two 128-row tiles A and
 // B, each owned by a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row
-// t of its tile = TMEM lane t), plus an issuer warp (warp 8) whose first thread issues every TMA
-// load and every tcgen05.mma. Keys come in tiles of 64 through a 3-stage TMA ring shared by both
-// query tiles. Per key tile j and query tile X:
-//   S_X(j) = Q_X K(j)^T  8 MMAs (M 128, N 64, K 16) into TMEM S_X[j & 1] (64 columns);
-//   softmax               the warpgroup reads its rows of S_X(j) (tcgen05.ld, two passes: max,
-//                         then exp2 / sum / P), writes P in the input dtype to an SW128 K-major
-//                         shared tile (bf16: plus its rounding residue to a second tile);
-//   O_X += P V(j)          4 MMAs (M 128, N 128, K 16) into TMEM O_X, V read MN-major straight from
-//                         its TMA layout.
-// O never leaves TMEM until the end: a row is rescaled in place (tcgen05.ld / st) only when its
-// running maximum grows by more than 8 in the exp2 domain, so P stays below 2^8. While one
-// warpgroup runs its softmax the tensor pipe works on the other tile's MMAs. Every wait is
-// bounded: a timeout is recorded, the CTA stops issuing, drains its own loads (bounded), frees
-// TMEM and returns without writing.
+// t of its tile = TMEM lane t), an MMA warp (warp 8) whose first thread issues every tcgen05.mma,
+// and a load warp (warp 9) whose first thread issues every TMA load. Keys come in tiles of 64
+// through a 5-stage TMA ring shared by both query tiles; the load thread refills a stage as soon
+// as the MMAs that read it have completed, so the MMA thread never waits on a refill. Per key
+// tile j and query tile X:
+//   S_X(j) = Q_X K(j)^T  8 MMAs (M 128, N 64, K 16) into TMEM S_X[j & 1] (64 fp32 columns);
+//   softmax               the warpgroup reads its rows of S_X(j) in one tcgen05.ld, computes
+//                         exp2 / sum, and writes P in the input dtype back over S_X(j) in TMEM
+//                         (32 columns of b16 pairs; bf16: its rounding residue in the other 32);
+//   O_X += P V(j)          4 MMAs (M 128, N 128, K 16; bf16: 8) into TMEM O_X with A = P read from
+//                         TMEM and B = V read MN-major straight from its TMA layout.
+// MMAs issued by one thread run in issue order, so S_X(j + 2), issued after O_X += P V(j), cannot
+// overwrite P_X(j) before it is read. O never leaves TMEM until the end: a row is rescaled in place
+// (tcgen05.ld / st) only when its running maximum grows by more than 8 in the exp2 domain, so P
+// stays below 2^8, and only then does the softmax wait for the previous P V. While one warpgroup
+// runs its softmax the tensor pipe works on the other tile's MMAs. Every wait is bounded: a
+// timeout is recorded, the CTA stops issuing, drains its own loads (bounded), frees TMEM and
+// returns without writing.
 constexpr int kTM = 128;                 // query rows per tile (two tiles per CTA)
 constexpr int kTN = 64;                  // keys per tile
-constexpr int kTThreads = 9 * 32;        // 2 softmax warpgroups + the issuer warp
+constexpr int kTThreads = 11 * 32;       // 2 softmax warpgroups, the MMA warps of tiles A and B, the load warp
 constexpr int kQHalf = kTM * 128;        // one SW128 box of Q: 128 rows x 64 elements (16 KiB)
 constexpr int kKHalf = kTN * 128;        // one SW128 box of K or V: 64 rows x 64 elements (8 KiB)
 constexpr uint32_t kTmemCols = 512;      // S_A[2], S_B[2] (64 each), O_A, O_B (128 each)
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 constexpr float kRescaleAbove = 8.f;     // exp2 domain
 
-// Shared-memory layout per element type: bf16 keeps a second P tile per query tile (the
-// rounding residue of P) and a 3-stage K/V ring; fp16 needs no residue and uses the room for a
-// 4-stage ring.
-template <bool kSplitP>
+// Shared-memory layout: Q_A and Q_B, then the K and V stages (P lives in TMEM).
 struct TcLayout {
-  static constexpr int kStages = kSplitP ? 3 : 4;
+  static constexpr int kStages = 5;
   static constexpr int kOffQ = 0;                                   // Q_A, Q_B: 2 halves each
   static constexpr int kOffK = kOffQ + 4 * kQHalf;                  // stage s: 2 halves
   static constexpr int kOffV = kOffK + kStages * 2 * kKHalf;        // stage s: 2 halves
-  static constexpr int kOffP = kOffV + kStages * 2 * kKHalf;        // P_A, P_B: 128 rows x 64 keys
-  static constexpr int kOffPl = kOffP + 2 * kQHalf;                 // bf16 residues of P_A, P_B
-  static constexpr int kOffBar = kOffPl + (kSplitP ? 2 * kQHalf : 0);
-  static constexpr int kSmem = kOffBar + 256 + 1024;                // + 1024-byte alignment slack
+  static constexpr int kOffBar = kOffV + kStages * 2 * kKHalf;
+  static constexpr int kSmem = kOffBar + 512 + 1024;                // + 1024-byte alignment slack
 };
+static_assert(TcLayout::kSmem <= 232448, "prefill smem above the 227 KB per-CTA limit");
 
-// mbarrier slots (K/V slots sized for up to 4 stages)
-constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = 5, kBarKFree = 9, kBarVFree = 13, kBarSFull = 17,  // S: [X][buf]
-    kBarPFull = 21, kBarPv = 23, kBarDrain = 25, kBarCount = 26;
+// mbarrier slots
+constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = kBarKFull + TcLayout::kStages,
+              kBarKFree = kBarVFull + TcLayout::kStages, kBarVFree = kBarKFree + TcLayout::kStages,
+              kBarSFull = kBarVFree + TcLayout::kStages,  // S: [X][buf]
+    kBarPFull = kBarSFull + 4, kBarPv = kBarPFull + 2, kBarDrain = kBarPv + 2, kBarCount = kBarDrain + 2;
+static_assert(8 * kBarCount + 8 <= 512, "mbarrier slots, the TMEM address and the abort flag fit the barrier area");
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
@@ -111,12 +117,21 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
+// The same with A read from TMEM (K-major: row i in lane i, two 16-bit elements per column).
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // OR of `v` over the 128 threads of named barrier `id` (a barrier itself: every thread must come).
 __device__ __forceinline__ bool group_any(int id, bool v) {
   uint32_t r;
@@ -153,6 +168,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 }
 
 
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 // The 64 fp32 columns of this thread's TMEM lane starting at `taddr`, in one round trip: the load
 // and its wait are one statement, so no use of the registers can be placed before the wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
@@ -173,8 +194,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                   const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t o_stride,
                   const int32_t* __restrict__ cu_seqlens, int64_t num_tokens, int max_seqlen, int G,
                   float scale_log2) {
-  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
-  using LY = TcLayout<kSplitP>;
+  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;  // P as value + rounding residue
+  using LY = TcLayout;
   constexpr int kSt = LY::kStages;
   extern __shared__ uint8_t tsmem_raw[];
   const uint32_t raw = smem_u32(tsmem_raw);
@@ -206,6 +227,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
   if (tid == 0) {
     for (int i = 0; i < kBarCount; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < kSt; ++i) {  // a stage is released by both query tiles' MMA threads
+      mbar_init(&bars[kBarKFree + i], 2);
+      mbar_init(&bars[kBarVFree + i], 2);
+    }
     fence_mbar_init();
     *s_abort = 0;
   }
@@ -225,15 +250,12 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   auto sQx = [&](int x) { return sQ + static_cast<uint32_t>(x) * 2 * kQHalf; };
   auto sK = [&](int st) { return base + LY::kOffK + static_cast<uint32_t>(st) * 2 * kKHalf; };
   auto sV = [&](int st) { return base + LY::kOffV + static_cast<uint32_t>(st) * 2 * kKHalf; };
-  auto sP = [&](int x) { return base + LY::kOffP + static_cast<uint32_t>(x) * kQHalf; };
-  auto sPl = [&](int x) { return base + LY::kOffPl + static_cast<uint32_t>(x) * kQHalf; };
 
   bool abort = false;
-  if (warp == 8) {
-    // ------------------------------- issuer -------------------------------
-    // Per key tile j, for query tile A then B: as soon as softmax x has published P_x(j), the
-    // scores S_x(j + 1) and then O_x += P_x V(j), so that each warpgroup's next scores follow its
-    // own softmax and do not wait for the other warpgroup's.
+  if (warp == 9) {
+    // ------------------------------- loads -------------------------------
+    // Q_A, Q_B and the first kSt key tiles at once; then tile t into the stage of tile t - kSt as
+    // soon as the MMAs that read that tile have completed.
     if ((tid & 31) == 0) {
       auto issue_kv = [&](int t) {
         const int st = t % kSt;
@@ -254,97 +276,107 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       }
       int issued = 0;
       for (; issued < min(kSt, n_tiles); ++issued) issue_kv(issued);
+      bool ok = true;
+      for (; issued < n_tiles; ++issued) {
+        const int pt = issued - kSt;  // the tile whose stage this load reuses
+        const uint32_t pph = static_cast<uint32_t>((pt / kSt) & 1);
+        ok = !*s_abort && mbar_wait_bounded(&bars[kBarKFree + pt % kSt], pph, kTcWaitNs) &&
+             mbar_wait_bounded(&bars[kBarVFree + pt % kSt], pph, kTcWaitNs);
+        if (!ok) break;
+        issue_kv(issued);
+      }
+      // The last kSt loads may still be in flight (earlier ones were consumed before their stage
+      // was reused): the CTA does not exit before they land, bounded.
+      if (!mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs)) ok = false;
+      for (int t = max(0, issued - kSt); t < issued; ++t) {
+        const uint32_t ph = static_cast<uint32_t>((t / kSt) & 1);
+        if (!mbar_wait_bounded(&bars[kBarKFull + t % kSt], ph, kTcWaitNs)) ok = false;
+        if (!mbar_wait_bounded(&bars[kBarVFull + t % kSt], ph, kTcWaitNs)) ok = false;
+      }
+      if (!ok) {
+        *s_abort = 1;
+        __threadfence_block();
+      }
+      abort = !ok;
+    }
+  } else if (warp == 8 || warp == 10) {
+    // ------------------------------- MMA issue, query tile x -------------------------------
+    // Each query tile has its own MMA thread (warps 8 and 10 sit on different SM sub-partitions),
+    // so the two tiles' MMAs are issued in parallel and neither waits behind the other. The
+    // scores run two key tiles ahead of the softmax: S_x(0) and S_x(1) first, then, as soon as
+    // softmax x has published P_x(j), O_x += P_x V(j) and the scores S_x(j + 2) into the buffer
+    // that P_x(j) occupies (the P V ahead of it in this thread's issue order has read P_x(j) by
+    // then). So a softmax warpgroup finds its next scores ready when it has published P, and
+    // waits for this thread only through the previous P V. A key tile's stage goes back to the
+    // load thread after two arrivals: one commit per query tile that reads it, and a plain
+    // arrival from the tile's MMA thread for a query tile that does not.
+    const int x = warp == 8 ? 0 : 1;
+    const int nx = x == 0 ? nA : nB;
+    const int n_other = x == 0 ? nB : nA;
+    if ((tid & 31) == 0 && nx > 0) {
       const uint32_t id_s = idesc_f16<T>(kTN, false), id_o = idesc_f16<T>(128, true);
       bool ok = mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs);
-      int k_seen = 0, v_seen = 0;  // key tiles whose K / V loads were seen landing
-      auto wait_k = [&](int t) {
-        ok = ok && mbar_wait_bounded(&bars[kBarKFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
-        if (ok) k_seen = t + 1;
+      // K(t) / V(t) are waited for by both MMA threads; the second wait finds the same phase
+      // complete, because the stage is not refilled before both have released it.
+      auto wait_kv = [&](int base_bar, int t) {
+        ok = ok && !*s_abort &&
+             mbar_wait_bounded(&bars[base_bar + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
       };
-      // S_x(t) into S_x[t & 1]. That buffer last held S_x(t - 2), which softmax x read before it
-      // published P_x(t - 1), which this thread waited for before issuing S_x(t).
-      auto issue_s = [&](int x, int t) {
+      // S_x(t) into S_x[t & 1]. That buffer last held P_x(t - 2), read by O_x += P_x V(t - 2),
+      // which this thread issued just before S_x(t).
+      const uint32_t dq = static_cast<uint32_t>(x) * 2 * kQHalf;
+      auto issue_s = [&](int t) {
         const int st = t % kSt;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t qo = static_cast<uint32_t>(kk >> 2) * kQHalf + static_cast<uint32_t>(kk & 3) * 32;
           const uint32_t ko = static_cast<uint32_t>(kk >> 2) * kKHalf + static_cast<uint32_t>(kk & 3) * 32;
-          umma_f16(tmem_s(x, t & 1), sw128_desc(sQx(x) + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
+          umma_f16(tmem_s(x, t & 1), sw128_desc(sQ + dq + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
                    kk > 0);
         }
         umma_commit(bar_u32(kBarSFull + x * 2 + (t & 1)));
       };
-      if (n_tiles > 0) {
-        wait_k(0);
-        if (ok) {
-          tc_fence_after();
-          issue_s(0, 0);
-          if (nB > 0) issue_s(1, 0);
-        }
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kSt;
-        const uint32_t ph = static_cast<uint32_t>((j / kSt) & 1);
-        // refill the stage of tile j - 1 (all its readers were issued by the end of iteration j - 1)
-        if (j >= 1 && issued < n_tiles) {
-          const int ps = (j - 1) % kSt;
-          const uint32_t pph = static_cast<uint32_t>(((j - 1) / kSt) & 1);
-          ok = mbar_wait_bounded(&bars[kBarKFree + ps], pph, kTcWaitNs) &&
-               mbar_wait_bounded(&bars[kBarVFree + ps], pph, kTcWaitNs);
-          if (!ok) break;
-          issue_kv(issued++);
-        }
-        ok = mbar_wait_bounded(&bars[kBarVFull + st], ph, kTcWaitNs);
+      for (int t = 0; t < min(2, nx) && ok; ++t) {
+        wait_kv(kBarKFull, t);
         if (!ok) break;
-        v_seen = j + 1;
-        if (j + 1 < n_tiles) {
-          wait_k(j + 1);
-          if (!ok) break;
-        }
         tc_fence_after();
-        for (int x = 0; x < 2; ++x) {
-          const int nx = x == 0 ? nA : nB;
-          if (j >= nx) continue;
-          ok = mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
-          if (!ok) break;
-          tc_fence_after();
-          // S_x(j + 1) ahead of O_x += P_x V(j): softmax x computes its next maximum while the
-          // P V MMAs run, and waits for them only before it rescales O_x and rewrites P_x.
-          if (j + 1 < nx) issue_s(x, j + 1);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            umma_f16(tmem_o(x), sw128_desc(sP(x) + kk * 32, 16, 1024), sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (kSplitP)
-              umma_f16(tmem_o(x), sw128_desc(sPl(x) + kk * 32, 16, 1024), sw128_desc(sV(st) + kk * 2048, kKHalf, 1024),
-                       id_o, 1u);
-          }
-          umma_commit(bar_u32(kBarPv + x));
-        }
-        if (!ok) break;
-        umma_commit(bar_u32(kBarKFree + st));  // K(j) was read by S(j), issued before this point
-        umma_commit(bar_u32(kBarVFree + st));
+        issue_s(t);
       }
-      if (ok && n_tiles > 0) {  // the last tile's release commits have landed before the CTA exits
-        const int t = n_tiles - 1;
-        const uint32_t tph = static_cast<uint32_t>((t / kSt) & 1);
-        ok = mbar_wait_bounded(&bars[kBarKFree + t % kSt], tph, kTcWaitNs) &&
-             mbar_wait_bounded(&bars[kBarVFree + t % kSt], tph, kTcWaitNs);
+      for (int j = 0; j < nx && ok; ++j) {
+        const int st = j % kSt;
+        ok = !*s_abort && mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
+        wait_kv(kBarVFull, j);
+        if (j + 2 < nx) wait_kv(kBarKFull, j + 2);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t pa = tmem_s(x, j & 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          umma_f16_ts(tmem_o(x), pa + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (kSplitP)
+            umma_f16_ts(tmem_o(x), pa + 32 + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o, 1u);
+        }
+        umma_commit(bar_u32(kBarPv + x));
+        if (j + 2 < nx) issue_s(j + 2);
+        // K(j) was read by S_x(j) and V(j) by O_x += P_x V(j), both issued before this point
+        umma_commit(bar_u32(kBarKFree + st));
+        umma_commit(bar_u32(kBarVFree + st));
+        if (j >= n_other) {
+          mbar_arrive(&bars[kBarKFree + st]);
+          mbar_arrive(&bars[kBarVFree + st]);
+        }
       }
       // every MMA this thread issued has completed before TMEM is freed
-      umma_commit(bar_u32(kBarDrain));
-      if (!mbar_wait_bounded(&bars[kBarDrain], 0, kTcWaitNs)) ok = false;
+      umma_commit(bar_u32(kBarDrain + x));
+      if (!mbar_wait_bounded(&bars[kBarDrain + x], 0, kTcWaitNs)) ok = false;
       if (!ok) {
         *s_abort = 1;
         __threadfence_block();
-        atomicOr(&g_deverr_prefill, AEG_DEVERR_WAIT_TIMEOUT);
-        // loads issued but not seen landing: wait (bounded) before the CTA can exit
-        for (int t = k_seen; t < issued; ++t)
-          mbar_wait_bounded(&bars[kBarKFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
-        for (int t = v_seen; t < issued; ++t)
-          mbar_wait_bounded(&bars[kBarVFull + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
-        // release the softmax warpgroups from any wait on this thread
-        for (int i = kBarSFull; i < kBarDrain; ++i) mbar_arrive(&bars[i]);
+        // release softmax x from any wait on this thread
+        mbar_arrive(&bars[kBarSFull + x * 2]);
+        mbar_arrive(&bars[kBarSFull + x * 2 + 1]);
+        mbar_arrive(&bars[kBarPv + x]);
       }
       abort = !ok;
     }
@@ -391,8 +423,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         mx *= scale_log2;
       }
-      // P_x is free and O_x stable once O_x += P_x V(j - 1) has completed
-      if (j > 0 && !bad) {
+      const bool grow = mx > m_used + kRescaleAbove;
+      const float factor = grow ? ex2p(m_used - mx) : 1.f;  // 0 while the row has seen nothing
+      // O_x += P_x V(j - 1) is waited for once per key tile, between S_x(j) landing and P_x(j)
+      // being published: S_x(j) was issued after O_x += P_x V(j - 2) and O_x += P_x V(j) is issued
+      // only after the publication, so the barrier's pending phase is j - 1 or j and the parity
+      // wait is exact. The wait also keeps this warpgroup at most one publication ahead of the
+      // MMA thread. O rows are rescaled in TMEM by the whole warp when any of its rows needs it,
+      // which needs that P V done first; otherwise the wait comes after the P stores.
+      const bool rescale = !bad && j > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY);
+      if (rescale) {
         bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
         bad = __any_sync(0xffffffffu, bad);
       }
@@ -403,11 +443,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
         continue;
       }
-      tc_fence_after();
-      const bool grow = mx > m_used + kRescaleAbove;
-      const float factor = grow ? ex2p(m_used - mx) : 1.f;  // 0 while the row has seen nothing
-      // O rows are rescaled in TMEM by the whole warp when any of its rows needs it
-      if (j > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
+      if (rescale) {
+        tc_fence_after();
         const uint32_t to = tmem_o(x) + lane_off;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -425,7 +462,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       }
       const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
       float rsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
-      const uint32_t roff = static_cast<uint32_t>(r) * 128;
+      const uint32_t tp = tmem_s(x, j & 1) + lane_off;  // P_x(j) over S_x(j): keys 2c, 2c + 1 in column c
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[8], pr[8];
@@ -440,23 +477,18 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             pr[i >> 1] = pack2<T>(p0 - rr.x, p1 - rr.y);
           }
         }
-        // keys c*16 .. c*16+15 of row r: 16-byte chunks 2c and 2c + 1 of the row, swizzled
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const uint32_t chunk = (static_cast<uint32_t>(c * 2 + q2) ^ static_cast<uint32_t>(r & 7)) * 16;
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sP(x) + roff + chunk), "r"(pk[4 * q2]),
-                       "r"(pk[4 * q2 + 1]), "r"(pk[4 * q2 + 2]), "r"(pk[4 * q2 + 3])
-                       : "memory");
-          if constexpr (kSplitP)
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sPl(x) + roff + chunk), "r"(pr[4 * q2]),
-                         "r"(pr[4 * q2 + 1]), "r"(pr[4 * q2 + 2]), "r"(pr[4 * q2 + 3])
-                         : "memory");
-        }
+        tmem_st8(tp + c * 8, pk);  // keys c*16 .. c*16+15
+        if constexpr (kSplitP) tmem_st8(tp + 32 + c * 8, pr);
       }
       l += (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
-      fence_async_smem();
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      bool late = false;
+      if (j > 0 && !rescale) {
+        late = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
+        late = __any_sync(0xffffffffu, late);
+      }
       tc_fence_before();
-      if (group_any(1 + x, false)) {  // P published by all four warps, unless one of them gave up
+      if (group_any(1 + x, late)) {  // P published by all four warps, unless one of them gave up
         abort = true;
         break;
       }
@@ -548,13 +580,13 @@ int launch_prefill_tc(void* out, int64_t o_stride, const void* q, int64_t q_stri
     std::lock_guard<std::mutex> lock(mu);
     if (!configured[dev]) {
       AEG_CHECK_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcLayout<std::is_same<T, __nv_bfloat16>::value>::kSmem));
+                                         TcLayout::kSmem));
       configured[dev] = true;
     }
   }
   const dim3 grid(static_cast<unsigned>(Hq), static_cast<unsigned>(B),
                   static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)));
-  prefill_tc_kernel<T><<<grid, kTThreads, TcLayout<std::is_same<T, __nv_bfloat16>::value>::kSmem, stream>>>(
+  prefill_tc_kernel<T><<<grid, kTThreads, TcLayout::kSmem, stream>>>(
       qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, max_seqlen, Hq / Hkv,
       static_cast<float>(static_cast<double>(scale) * 1.4426950408889634));
   AEG_CHECK_LAUNCH("prefill_attention(tcgen05)");
