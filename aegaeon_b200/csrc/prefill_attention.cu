@@ -24,6 +24,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -70,23 +72,41 @@ constexpr uint32_t kTmemCols = 512;      // S_A[2], S_B[2] (64 each), O_A, O_B (
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 constexpr float kRescaleAbove = 8.f;     // exp2 domain
 
-// Shared-memory layout: Q_A and Q_B, then the K and V stages (P lives in TMEM).
+// Shared-memory layout: Q_A and Q_B, the K and V stages, and a 4 KiB output staging tile per
+// softmax warp (P lives in TMEM).
 struct TcLayout {
-  static constexpr int kStages = 5;
+  static constexpr int kStages = 4;
   static constexpr int kOffQ = 0;                                   // Q_A, Q_B: 2 halves each
   static constexpr int kOffK = kOffQ + 4 * kQHalf;                  // stage s: 2 halves
   static constexpr int kOffV = kOffK + kStages * 2 * kKHalf;        // stage s: 2 halves
-  static constexpr int kOffBar = kOffV + kStages * 2 * kKHalf;
+  static constexpr int kOffE = kOffV + kStages * 2 * kKHalf;        // warp w: 32 rows x 128 bytes
+  static constexpr int kOffBar = kOffE + 8 * 4096;
   static constexpr int kSmem = kOffBar + 512 + 1024;                // + 1024-byte alignment slack
 };
 static_assert(TcLayout::kSmem <= 232448, "prefill smem above the 227 KB per-CTA limit");
 
-// mbarrier slots
-constexpr int kBarQ = 0, kBarKFull = 1, kBarVFull = kBarKFull + TcLayout::kStages,
+// mbarrier slots. QFull: the item record and its Q landed; QFree: every warp is done with them
+// (both MMA threads after their last S, each softmax warp after reading the record).
+constexpr int kBarQFull = 0, kBarQFree = 1, kBarKFull = 2, kBarVFull = kBarKFull + TcLayout::kStages,
               kBarKFree = kBarVFull + TcLayout::kStages, kBarVFree = kBarKFree + TcLayout::kStages,
               kBarSFull = kBarVFree + TcLayout::kStages,  // S: [X][buf]
-    kBarPFull = kBarSFull + 4, kBarPv = kBarPFull + 2, kBarDrain = kBarPv + 2, kBarCount = kBarDrain + 2;
-static_assert(8 * kBarCount + 8 <= 512, "mbarrier slots, the TMEM address and the abort flag fit the barrier area");
+    kBarPFull = kBarSFull + 4, kBarPv = kBarPFull + 2, kBarOFree = kBarPv + 2, kBarDrain = kBarOFree + 2,
+              kBarCount = kBarDrain + 2;
+constexpr int kQFreeArrivals = 2 + 8;
+
+// One work item: query tiles A and B (rows q0 .. q0 + 255) of head h of the prompt at s0 of
+// length L, with nA / nB key tiles; nA < 0 marks the end of the work.
+struct PfItem {
+  int s0, L, h, q0, nA, nB;
+};
+static_assert(8 * kBarCount + 8 + sizeof(PfItem) <= 512,
+              "mbarrier slots, the TMEM address, the abort flag and the item record fit the barrier area");
+
+// Work counters: each launch takes one of kCounterSlots (round robin on the host), its CTAs take
+// items with atomicAdd, and the last CTA to run out of work sets both back to zero.
+constexpr int kCounterSlots = 64;
+__device__ unsigned int g_pf_next[kCounterSlots];
+__device__ unsigned int g_pf_done[kCounterSlots];
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
@@ -132,6 +152,19 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Non-blocking probe of an mbarrier phase (mbarrier.test_wait returns at once).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // OR of `v` over the 128 threads of named barrier `id` (a barrier itself: every thread must come).
 __device__ __forceinline__ bool group_any(int id, bool v) {
   uint32_t r;
@@ -174,6 +207,19 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                : "memory");
 }
 
+// 32 fp32 columns of this thread's TMEM lane, load and wait in one statement.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // The 64 fp32 columns of this thread's TMEM lane starting at `taddr`, in one round trip: the load
 // and its wait are one statement, so no use of the registers can be placed before the wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
@@ -192,8 +238,8 @@ template <typename T>
 __global__ void __launch_bounds__(kTThreads, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t o_stride,
-                  const int32_t* __restrict__ cu_seqlens, int64_t num_tokens, int max_seqlen, int G,
-                  float scale_log2) {
+                  const int32_t* __restrict__ cu_seqlens, int64_t num_tokens, int B, int Hq, int levels,
+                  int max_seqlen, int G, float scale_log2, int slot) {
   constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;  // P as value + rounding residue
   using LY = TcLayout;
   constexpr int kSt = LY::kStages;
@@ -203,30 +249,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   uint8_t* smem = tsmem_raw + (base - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::kOffBar + 8 * kBarCount);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + LY::kOffBar + 8 * kBarCount + 4);  // the issuer gave up
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + LY::kOffBar + 8 * kBarCount + 4);  // a wait gave up
+  volatile PfItem* s_item = reinterpret_cast<volatile PfItem*>(smem + LY::kOffBar + 8 * kBarCount + 8);
   auto bar_u32 = [&](int i) { return base + LY::kOffBar + 8u * static_cast<uint32_t>(i); };
-
-  // Blocks start in linear order (x fastest): the query-tile level is the outermost dimension,
-  // heaviest (last) tiles first over every prompt and head, so the lightest CTAs fill the tail.
-  const int tile_m = static_cast<int>(gridDim.z) - 1 - static_cast<int>(blockIdx.z);
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int s0 = cu_seqlens[b];
-  const int L = cu_seqlens[b + 1] - s0;
-  if (s0 < 0 || L < 0 || static_cast<int64_t>(s0) + L > num_tokens || L > max_seqlen) {
-    if (threadIdx.x == 0 && blockIdx.z == 0 && h == 0) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
-    return;
-  }
-  const int q0 = tile_m * 2 * kTM;
-  if (L == 0 || q0 >= L) return;
-  const int kvh = h / G;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const bool has_b = q0 + kTM < L;
-  const int nA = (min(L, q0 + kTM) + kTN - 1) / kTN;                  // key tiles tile A needs
-  const int nB = has_b ? (min(L, q0 + 2 * kTM) + kTN - 1) / kTN : 0;  // and tile B
-  const int n_tiles = has_b ? nB : nA;
 
   if (tid == 0) {
     for (int i = 0; i < kBarCount; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&bars[kBarQFree], kQFreeArrivals);
     for (int i = 0; i < kSt; ++i) {  // a stage is released by both query tiles' MMA threads
       mbar_init(&bars[kBarKFree + i], 2);
       mbar_init(&bars[kBarVFree + i], 2);
@@ -253,45 +283,133 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
   bool abort = false;
   if (warp == 9) {
-    // ------------------------------- loads -------------------------------
-    // Q_A, Q_B and the first kSt key tiles at once; then tile t into the stage of tile t - kSt as
-    // soon as the MMAs that read that tile have completed.
+    // ------------------------------- work items and loads -------------------------------
+    // Items are (query-tile level, prompt, head), heaviest level first, taken from the launch's
+    // counter. The next item is fetched while the current one computes; its Q and the item
+    // record go out once every warp is done with the current item's (QFree), its key tiles into
+    // the ring as the MMA threads release stages.
     if ((tid & 31) == 0) {
-      auto issue_kv = [&](int t) {
-        const int st = t % kSt;
-        const int y = s0 + t * kTN, x = kvh * 128;
-        mbar_arrive_expect_tx(&bars[kBarKFull + st], 2 * kKHalf);
-        tma_load_2d(sK(st), &kmap, bar_u32(kBarKFull + st), x, y);
-        tma_load_2d(sK(st) + kKHalf, &kmap, bar_u32(kBarKFull + st), x + 64, y);
-        mbar_arrive_expect_tx(&bars[kBarVFull + st], 2 * kKHalf);
-        tma_load_2d(sV(st), &vmap, bar_u32(kBarVFull + st), x, y);
-        tma_load_2d(sV(st) + kKHalf, &vmap, bar_u32(kBarVFull + st), x + 64, y);
+      const unsigned per_level = static_cast<unsigned>(B) * static_cast<unsigned>(Hq);
+      const unsigned total = per_level * static_cast<unsigned>(levels);
+      auto fetch = [&](PfItem& it) {
+        it.nA = -1;
+        while (!*s_abort) {
+          const unsigned i = atomicAdd(&g_pf_next[slot], 1u);
+          if (i >= total) return;
+          const int lv = static_cast<int>(i / per_level);
+          const int rem = static_cast<int>(i % per_level);
+          const int b = rem / Hq, h = rem % Hq;
+          const int q0 = (levels - 1 - lv) * 2 * kTM;
+          const int s0 = cu_seqlens[b];
+          const int L = cu_seqlens[b + 1] - s0;
+          const bool valid = s0 >= 0 && L >= 0 && static_cast<int64_t>(s0) + L <= num_tokens && L <= max_seqlen;
+          if (!valid) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
+          if (!valid || L == 0 || q0 >= L) {
+            // every head of this (level, prompt) is empty: move the counter past them
+            atomicMax(&g_pf_next[slot], static_cast<unsigned>(lv) * per_level + static_cast<unsigned>(b + 1) * Hq);
+            continue;
+          }
+          it.s0 = s0;
+          it.L = L;
+          it.h = h;
+          it.q0 = q0;
+          it.nA = (min(L, q0 + kTM) + kTN - 1) / kTN;
+          it.nB = q0 + kTM < L ? (min(L, q0 + 2 * kTM) + kTN - 1) / kTN : 0;
+          return;
+        }
       };
-      mbar_arrive_expect_tx(&bars[kBarQ], (has_b ? 4 : 2) * kQHalf);
-      tma_load_2d(sQx(0), &qmap, bar_u32(kBarQ), h * 128, s0 + q0);
-      tma_load_2d(sQx(0) + kQHalf, &qmap, bar_u32(kBarQ), h * 128 + 64, s0 + q0);
-      if (has_b) {
-        tma_load_2d(sQx(1), &qmap, bar_u32(kBarQ), h * 128, s0 + q0 + kTM);
-        tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQ), h * 128 + 64, s0 + q0 + kTM);
-      }
-      int issued = 0;
-      for (; issued < min(kSt, n_tiles); ++issued) issue_kv(issued);
+      // One polling loop: the next item's record and Q go out as soon as every warp is done with
+      // the previous ones (its tiles are issued by then: the last S of an item reads its last
+      // key tile), and key tiles are issued in ring order as stages come free. The item after
+      // that is fetched right after a publication, while the current one computes.
+      PfItem nxt;
+      fetch(nxt);
+      // Published items whose key tiles are not all issued: at most two (an item is published
+      // only after the previous one's last key tile has landed), the older in p0.
+      struct Pending {
+        int g0, n, s0, kvh;
+      } p0{0, 0, 0, 0}, p1{0, 0, 0, 0};
+      int n_pend = 0;
+      int k = 0;              // items published
+      int t_next = 0;         // key tiles issued so far (over all items)
+      int t_end = 0;          // key tiles of the published items
+      bool published_end = false;
       bool ok = true;
-      for (; issued < n_tiles; ++issued) {
-        const int pt = issued - kSt;  // the tile whose stage this load reuses
-        const uint32_t pph = static_cast<uint32_t>((pt / kSt) & 1);
-        ok = !*s_abort && mbar_wait_bounded(&bars[kBarKFree + pt % kSt], pph, kTcWaitNs) &&
-             mbar_wait_bounded(&bars[kBarVFree + pt % kSt], pph, kTcWaitNs);
-        if (!ok) break;
-        issue_kv(issued);
+      uint64_t idle_since = 0;
+      while (ok && !(published_end && t_next == t_end)) {
+        bool progressed = false;
+        if (!published_end && (k == 0 || mbar_test(&bars[kBarQFree], static_cast<uint32_t>((k - 1) & 1)))) {
+          s_item->s0 = nxt.s0;
+          s_item->L = nxt.L;
+          s_item->h = nxt.h;
+          s_item->q0 = nxt.q0;
+          s_item->nA = nxt.nA;
+          s_item->nB = nxt.nB;
+          if (nxt.nA < 0) {  // no more work: the record alone
+            mbar_arrive(&bars[kBarQFull]);
+            published_end = true;
+          } else {
+            const PfItem it = nxt;
+            const int n_tiles = it.nB > 0 ? it.nB : it.nA;
+            mbar_arrive_expect_tx(&bars[kBarQFull], (it.nB > 0 ? 4 : 2) * kQHalf);
+            tma_load_2d(sQx(0), &qmap, bar_u32(kBarQFull), it.h * 128, it.s0 + it.q0);
+            tma_load_2d(sQx(0) + kQHalf, &qmap, bar_u32(kBarQFull), it.h * 128 + 64, it.s0 + it.q0);
+            if (it.nB > 0) {
+              tma_load_2d(sQx(1), &qmap, bar_u32(kBarQFull), it.h * 128, it.s0 + it.q0 + kTM);
+              tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQFull), it.h * 128 + 64, it.s0 + it.q0 + kTM);
+            }
+            (n_pend == 0 ? p0 : p1) = Pending{t_end, n_tiles, it.s0, it.h / G};
+            ++n_pend;
+            t_end += n_tiles;
+            ++k;
+            fetch(nxt);
+          }
+          progressed = true;
+        }
+        if (t_next < t_end) {
+          const int g = t_next;  // global tile g into stage g % kSt, after tile g - kSt's release
+          const uint32_t pph = static_cast<uint32_t>(((g - kSt) / kSt) & 1);
+          if (g < kSt || (mbar_test(&bars[kBarKFree + g % kSt], pph) && mbar_test(&bars[kBarVFree + g % kSt], pph))) {
+            const Pending pi = p0;
+            const int st = g % kSt, y = pi.s0 + (g - pi.g0) * kTN, xc = pi.kvh * 128;
+            mbar_arrive_expect_tx(&bars[kBarKFull + st], 2 * kKHalf);
+            tma_load_2d(sK(st), &kmap, bar_u32(kBarKFull + st), xc, y);
+            tma_load_2d(sK(st) + kKHalf, &kmap, bar_u32(kBarKFull + st), xc + 64, y);
+            mbar_arrive_expect_tx(&bars[kBarVFull + st], 2 * kKHalf);
+            tma_load_2d(sV(st), &vmap, bar_u32(kBarVFull + st), xc, y);
+            tma_load_2d(sV(st) + kKHalf, &vmap, bar_u32(kBarVFull + st), xc + 64, y);
+            ++t_next;
+            if (t_next == pi.g0 + pi.n) {
+              p0 = p1;
+              --n_pend;
+            }
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else {
+          const uint64_t now = globaltimer_ns();
+          if (idle_since == 0) idle_since = now;
+          if (now - idle_since > kTcWaitNs || *s_abort) ok = false;
+        }
       }
-      // The last kSt loads may still be in flight (earlier ones were consumed before their stage
-      // was reused): the CTA does not exit before they land, bounded.
-      if (!mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs)) ok = false;
-      for (int t = max(0, issued - kSt); t < issued; ++t) {
-        const uint32_t ph = static_cast<uint32_t>((t / kSt) & 1);
-        if (!mbar_wait_bounded(&bars[kBarKFull + t % kSt], ph, kTcWaitNs)) ok = false;
-        if (!mbar_wait_bounded(&bars[kBarVFull + t % kSt], ph, kTcWaitNs)) ok = false;
+      if (!ok && k > 0 && !published_end) {
+        // the last published item's Q may still be in flight: it lands before the CTA exits
+        mbar_wait_bounded(&bars[kBarQFull], static_cast<uint32_t>((k - 1) & 1), kTcWaitNs);
+      }
+      // The launch's counter goes back to zero once every CTA has run out of work.
+      __threadfence();
+      if (atomicAdd(&g_pf_done[slot], 1u) == gridDim.x - 1) {
+        atomicExch(&g_pf_next[slot], 0u);
+        atomicExch(&g_pf_done[slot], 0u);
+      }
+      // The last kSt key tiles may still be in flight (earlier ones were consumed before their
+      // stage was reused): they land before the CTA exits, bounded.
+      for (int g = max(0, t_next - kSt); g < t_next; ++g) {
+        const uint32_t ph = static_cast<uint32_t>((g / kSt) & 1);
+        if (!mbar_wait_bounded(&bars[kBarKFull + g % kSt], ph, kTcWaitNs)) ok = false;
+        if (!mbar_wait_bounded(&bars[kBarVFull + g % kSt], ph, kTcWaitNs)) ok = false;
       }
       if (!ok) {
         *s_abort = 1;
@@ -302,70 +420,91 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   } else if (warp == 8 || warp == 10) {
     // ------------------------------- MMA issue, query tile x -------------------------------
     // Each query tile has its own MMA thread (warps 8 and 10 sit on different SM sub-partitions),
-    // so the two tiles' MMAs are issued in parallel and neither waits behind the other. The
-    // scores run two key tiles ahead of the softmax: S_x(0) and S_x(1) first, then, as soon as
-    // softmax x has published P_x(j), O_x += P_x V(j) and the scores S_x(j + 2) into the buffer
-    // that P_x(j) occupies (the P V ahead of it in this thread's issue order has read P_x(j) by
-    // then). So a softmax warpgroup finds its next scores ready when it has published P, and
-    // waits for this thread only through the previous P V. A key tile's stage goes back to the
-    // load thread after two arrivals: one commit per query tile that reads it, and a plain
-    // arrival from the tile's MMA thread for a query tile that does not.
+    // so the two tiles' MMAs are issued in parallel and neither waits behind the other. Per item,
+    // the scores run two key tiles ahead of the softmax: S_x(0) and S_x(1) first, then, as soon
+    // as softmax x has published P_x(j), O_x += P_x V(j) and the scores S_x(j + 2) into the
+    // buffer that P_x(j) occupies (the P V ahead of it in this thread's issue order has read
+    // P_x(j) by then). The first P V of an item waits until softmax x has read O_x out for the
+    // previous item. A key tile's stage goes back to the load thread after two arrivals: one
+    // commit per query tile that reads it, and a plain arrival from the tile's MMA thread for a
+    // query tile that does not. Sequence numbers run over all items: gx counts this tile's key
+    // tiles (S buffer gx & 1, barrier phases), ex its items, t_base the ring's tiles.
     const int x = warp == 8 ? 0 : 1;
-    const int nx = x == 0 ? nA : nB;
-    const int n_other = x == 0 ? nB : nA;
-    if ((tid & 31) == 0 && nx > 0) {
+    if ((tid & 31) == 0) {
       const uint32_t id_s = idesc_f16<T>(kTN, false), id_o = idesc_f16<T>(128, true);
-      bool ok = mbar_wait_bounded(&bars[kBarQ], 0, kTcWaitNs);
-      // K(t) / V(t) are waited for by both MMA threads; the second wait finds the same phase
-      // complete, because the stage is not refilled before both have released it.
+      bool ok = true;
       auto wait_kv = [&](int base_bar, int t) {
         ok = ok && !*s_abort &&
              mbar_wait_bounded(&bars[base_bar + t % kSt], static_cast<uint32_t>((t / kSt) & 1), kTcWaitNs);
       };
-      // S_x(t) into S_x[t & 1]. That buffer last held P_x(t - 2), read by O_x += P_x V(t - 2),
-      // which this thread issued just before S_x(t).
-      const uint32_t dq = static_cast<uint32_t>(x) * 2 * kQHalf;
-      auto issue_s = [&](int t) {
-        const int st = t % kSt;
+      // S of sequence number g into S_x[g & 1] from ring tile tg. That buffer last held P of
+      // sequence g - 2, read by the P V this thread issued just before.
+      auto issue_s = [&](int g, int tg) {
+        const int st = tg % kSt;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t qo = static_cast<uint32_t>(kk >> 2) * kQHalf + static_cast<uint32_t>(kk & 3) * 32;
           const uint32_t ko = static_cast<uint32_t>(kk >> 2) * kKHalf + static_cast<uint32_t>(kk & 3) * 32;
-          umma_f16(tmem_s(x, t & 1), sw128_desc(sQ + dq + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
+          umma_f16(tmem_s(x, g & 1), sw128_desc(sQx(x) + qo, 16, 1024), sw128_desc(sK(st) + ko, 16, 1024), id_s,
                    kk > 0);
         }
-        umma_commit(bar_u32(kBarSFull + x * 2 + (t & 1)));
+        umma_commit(bar_u32(kBarSFull + x * 2 + (g & 1)));
       };
-      for (int t = 0; t < min(2, nx) && ok; ++t) {
-        wait_kv(kBarKFull, t);
+      int t_base = 0, gx = 0, ex = 0;
+      for (int k = 0; ok; ++k) {
+        ok = !*s_abort && mbar_wait_bounded(&bars[kBarQFull], static_cast<uint32_t>(k & 1), kTcWaitNs);
         if (!ok) break;
-        tc_fence_after();
-        issue_s(t);
-      }
-      for (int j = 0; j < nx && ok; ++j) {
-        const int st = j % kSt;
-        ok = !*s_abort && mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(j & 1), kTcWaitNs);
-        wait_kv(kBarVFull, j);
-        if (j + 2 < nx) wait_kv(kBarKFull, j + 2);
+        const int nA = s_item->nA, nB = s_item->nB;
+        if (nA < 0) break;
+        const int nx = x == 0 ? nA : nB;
+        const int n_other = x == 0 ? nB : nA;
+        const int n_tiles = nB > 0 ? nB : nA;
+        if (nx == 0) {  // no tile x in this item
+          mbar_arrive(&bars[kBarQFree]);
+          t_base += n_tiles;
+          continue;
+        }
+        for (int t = 0; t < min(2, nx) && ok; ++t) {
+          wait_kv(kBarKFull, t_base + t);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(gx + t, t_base + t);
+        }
         if (!ok) break;
-        tc_fence_after();
-        const uint32_t pa = tmem_s(x, j & 1);
+        if (nx <= 2) umma_commit(bar_u32(kBarQFree));  // Q_x is read by no later MMA of this item
+        for (int j = 0; j < nx && ok; ++j) {
+          const int g = gx + j, tg = t_base + j, st = tg % kSt;
+          ok = !*s_abort && mbar_wait_bounded(&bars[kBarPFull + x], static_cast<uint32_t>(g & 1), kTcWaitNs);
+          wait_kv(kBarVFull, tg);
+          if (j + 2 < nx) wait_kv(kBarKFull, tg + 2);
+          if (ok && j == 0 && ex > 0)
+            ok = mbar_wait_bounded(&bars[kBarOFree + x], static_cast<uint32_t>((ex - 1) & 1), kTcWaitNs);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t pa = tmem_s(x, g & 1);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          umma_f16_ts(tmem_o(x), pa + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-          if constexpr (kSplitP)
-            umma_f16_ts(tmem_o(x), pa + 32 + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o, 1u);
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_f16_ts(tmem_o(x), pa + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kSplitP)
+              umma_f16_ts(tmem_o(x), pa + 32 + kk * 8, sw128_desc(sV(st) + kk * 2048, kKHalf, 1024), id_o, 1u);
+          }
+          umma_commit(bar_u32(kBarPv + x));
+          if (j + 2 < nx) {
+            issue_s(g + 2, tg + 2);
+            if (j + 3 == nx) umma_commit(bar_u32(kBarQFree));  // that was the item's last S_x
+          }
+          // K(tg) was read by S_x and V(tg) by O_x += P_x V, both issued before this point
+          umma_commit(bar_u32(kBarKFree + st));
+          umma_commit(bar_u32(kBarVFree + st));
+          if (j >= n_other) {
+            mbar_arrive(&bars[kBarKFree + st]);
+            mbar_arrive(&bars[kBarVFree + st]);
+          }
         }
-        umma_commit(bar_u32(kBarPv + x));
-        if (j + 2 < nx) issue_s(j + 2);
-        // K(j) was read by S_x(j) and V(j) by O_x += P_x V(j), both issued before this point
-        umma_commit(bar_u32(kBarKFree + st));
-        umma_commit(bar_u32(kBarVFree + st));
-        if (j >= n_other) {
-          mbar_arrive(&bars[kBarKFree + st]);
-          mbar_arrive(&bars[kBarVFree + st]);
-        }
+        gx += nx;
+        ++ex;
+        t_base += n_tiles;
       }
       // every MMA this thread issued has completed before TMEM is freed
       umma_commit(bar_u32(kBarDrain + x));
@@ -384,143 +523,183 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     // ------------------------------- softmax warpgroup x -------------------------------
     const int x = warp >> 2;
     const int r = tid & 127;  // row of the tile, TMEM lane
-    const int row = q0 + x * kTM + r;
-    const int nx = x == 0 ? nA : nB;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
     // tcgen05.ld / st are warp-collective (.sync.aligned): a wait's outcome is made uniform over
     // the warp before the warp acts on it. The warpgroup meets once per key tile, at the barrier
     // that publishes P, which also votes on a timeout: a warp whose wait gave up skips its work
     // but still reaches that barrier, and then all four warps stop together.
-    bool bad = false;
-    for (int j = 0; j < nx; ++j) {
-      bad = bad || *s_abort ||
-            !mbar_wait_bounded(&bars[kBarSFull + x * 2 + (j & 1)], static_cast<uint32_t>((j >> 1) & 1), kTcWaitNs);
-      bad = __any_sync(0xffffffffu, bad);
-      // The row's 64 scores in one TMEM round trip. Keys this row cannot see become -inf; a key
-      // tile that every row of the query tile sees whole (uniform over the warpgroup) needs no
-      // mask. The scale is positive, so the row maximum is taken on the raw scores and scaled
-      // once, and each exponent below is one fused multiply-add.
-      const int key0 = j * kTN;
-      float sv[64];
-      float mx = -INFINITY;
-      if (!bad) {
-        tc_fence_after();
-        tmem_ld64(tmem_s(x, j & 1) + lane_off, sv);
-        if (!(key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L)) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int key = key0 + i;
-            sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
-          }
-        }
-        // eight independent partial maxima instead of one 64-long dependent chain
-        float mp[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mp[k] = sv[k];
-#pragma unroll
-        for (int i = 8; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
-        mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-        mx *= scale_log2;
-      }
-      const bool grow = mx > m_used + kRescaleAbove;
-      const float factor = grow ? ex2p(m_used - mx) : 1.f;  // 0 while the row has seen nothing
-      // O_x += P_x V(j - 1) is waited for once per key tile, between S_x(j) landing and P_x(j)
-      // being published: S_x(j) was issued after O_x += P_x V(j - 2) and O_x += P_x V(j) is issued
-      // only after the publication, so the barrier's pending phase is j - 1 or j and the parity
-      // wait is exact. The wait also keeps this warpgroup at most one publication ahead of the
-      // MMA thread. O rows are rescaled in TMEM by the whole warp when any of its rows needs it,
-      // which needs that P V done first; otherwise the wait comes after the P stores.
-      const bool rescale = !bad && j > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY);
-      if (rescale) {
-        bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
-        bad = __any_sync(0xffffffffu, bad);
-      }
-      if (bad) {  // this warp stops working; it still meets the others below
-        if (group_any(1 + x, true)) {
-          abort = true;
-          break;
-        }
-        continue;
-      }
-      if (rescale) {
-        tc_fence_after();
-        const uint32_t to = tmem_o(x) + lane_off;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float v[16];
-          tmem_ld16(to + c * 16, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] *= factor;
-          tmem_st16(to + c * 16, v);
-        }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      }
-      if (grow) {
-        l *= factor;
-        m_used = mx;
-      }
-      const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-      float rsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
-      const uint32_t tp = tmem_s(x, j & 1) + lane_off;  // P_x(j) over S_x(j): keys 2c, 2c + 1 in column c
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[8], pr[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float p0 = ex2p(fmaf(sv[c * 16 + i], scale_log2, neg_base));  // masked keys: ex2(-inf) = 0
-          const float p1 = ex2p(fmaf(sv[c * 16 + i + 1], scale_log2, neg_base));
-          rsum[(i >> 1) & 3] += p0 + p1;
-          pk[i >> 1] = pack2<T>(p0, p1);
-          if constexpr (kSplitP) {
-            const float2 rr = unpack2<T>(pk[i >> 1]);
-            pr[i >> 1] = pack2<T>(p0 - rr.x, p1 - rr.y);
-          }
-        }
-        tmem_st8(tp + c * 8, pk);  // keys c*16 .. c*16+15
-        if constexpr (kSplitP) tmem_st8(tp + 32 + c * 8, pr);
-      }
-      l += (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      bool late = false;
-      if (j > 0 && !rescale) {
-        late = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((j - 1) & 1), kTcWaitNs);
-        late = __any_sync(0xffffffffu, late);
-      }
-      tc_fence_before();
-      if (group_any(1 + x, late)) {  // P published by all four warps, unless one of them gave up
+    int gx = 0;  // key tiles of this query tile over all items (S buffer and barrier phases)
+    for (int k = 0; !abort; ++k) {
+      bool bad = *s_abort || !mbar_wait_bounded(&bars[kBarQFull], static_cast<uint32_t>(k & 1), kTcWaitNs);
+      if (group_any(1 + x, bad)) {
         abort = true;
         break;
       }
-      if (r == 0) mbar_arrive(&bars[kBarPFull + x]);
-    }
-    if (!abort && nx > 0) {
-      const bool bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((nx - 1) & 1), kTcWaitNs) || *s_abort;
-      abort = group_any(1 + x, bad);
-    }
-    tc_fence_after();
-    if (!abort && nx > 0) {  // warpgroup-uniform: the TMEM reads are collective, the stores per row
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* dst = out + static_cast<int64_t>(s0 + min(row, L - 1)) * o_stride + static_cast<int64_t>(h) * 128;
-      const uint32_t to = tmem_o(x) + lane_off;
+      const int s0 = s_item->s0, L = s_item->L, h = s_item->h, q0 = s_item->q0;
+      const int nA = s_item->nA, nB = s_item->nB;
+      __syncwarp();
+      if ((tid & 31) == 0) mbar_arrive(&bars[kBarQFree]);  // this warp has read the item record
+      if (nA < 0) break;
+      const int nx = x == 0 ? nA : nB;
+      if (nx == 0) continue;
+      const int row = q0 + x * kTM + r;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nx; ++j) {
+        const int g = gx + j;
+        bad = bad || *s_abort ||
+              !mbar_wait_bounded(&bars[kBarSFull + x * 2 + (g & 1)], static_cast<uint32_t>((g >> 1) & 1), kTcWaitNs);
+        bad = __any_sync(0xffffffffu, bad);
+        // The row's 64 scores in one TMEM round trip. Keys this row cannot see become -inf; a key
+        // tile that every row of the query tile sees whole (uniform over the warpgroup) needs no
+        // mask. The scale is positive, so the row maximum is taken on the raw scores and scaled
+        // once, and each exponent below is one fused multiply-add.
+        const int key0 = j * kTN;
+        float sv[64];
+        float mx = -INFINITY;
+        if (!bad) {
+          tc_fence_after();
+          tmem_ld64(tmem_s(x, g & 1) + lane_off, sv);
+          if (!(key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L)) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(to + c * 16, v);
-        uint4 w0, w1;
-        w0.x = pack2<T>(v[0] * inv, v[1] * inv);
-        w0.y = pack2<T>(v[2] * inv, v[3] * inv);
-        w0.z = pack2<T>(v[4] * inv, v[5] * inv);
-        w0.w = pack2<T>(v[6] * inv, v[7] * inv);
-        w1.x = pack2<T>(v[8] * inv, v[9] * inv);
-        w1.y = pack2<T>(v[10] * inv, v[11] * inv);
-        w1.z = pack2<T>(v[12] * inv, v[13] * inv);
-        w1.w = pack2<T>(v[14] * inv, v[15] * inv);
-        if (row < L) {
-          *reinterpret_cast<uint4*>(dst + c * 16) = w0;
-          *reinterpret_cast<uint4*>(dst + c * 16 + 8) = w1;
+            for (int i = 0; i < 64; ++i) {
+              const int key = key0 + i;
+              sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
+            }
+          }
+          // eight independent partial maxima instead of one 64-long dependent chain
+          float mp[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) mp[c] = sv[c];
+#pragma unroll
+          for (int i = 8; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
+          mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+          mx *= scale_log2;
+        }
+        const bool grow = mx > m_used + kRescaleAbove;
+        const float factor = grow ? ex2p(m_used - mx) : 1.f;  // 0 while the row has seen nothing
+        // The previous P V is waited for once per key tile, between S landing and P being
+        // published: S of sequence g was issued after the P V of g - 2 and the P V of g is issued
+        // only after the publication, so the barrier's pending phase is g - 1 or g and the parity
+        // wait is exact. The wait also keeps this warpgroup at most one publication ahead of the
+        // MMA thread. O rows are rescaled in TMEM by the whole warp when any of its rows needs it,
+        // which needs that P V done first; otherwise the wait comes after the P stores.
+        const bool rescale = !bad && j > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY);
+        if (rescale) {
+          bad = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((g - 1) & 1), kTcWaitNs);
+          bad = __any_sync(0xffffffffu, bad);
+        }
+        if (bad) {  // this warp stops working; it still meets the others below
+          if (group_any(1 + x, true)) {
+            abort = true;
+            break;
+          }
+          continue;
+        }
+        if (rescale) {
+          tc_fence_after();
+          const uint32_t to = tmem_o(x) + lane_off;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float v[16];
+            tmem_ld16(to + c * 16, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= factor;
+            tmem_st16(to + c * 16, v);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        if (grow) {
+          l *= factor;
+          m_used = mx;
+        }
+        const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
+        float rsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+        const uint32_t tp = tmem_s(x, g & 1) + lane_off;  // P over S: keys 2c, 2c + 1 in column c
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[8], pr[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float p0 = ex2p(fmaf(sv[c * 16 + i], scale_log2, neg_base));  // masked keys: ex2(-inf) = 0
+            const float p1 = ex2p(fmaf(sv[c * 16 + i + 1], scale_log2, neg_base));
+            rsum[(i >> 1) & 3] += p0 + p1;
+            pk[i >> 1] = pack2<T>(p0, p1);
+            if constexpr (kSplitP) {
+              const float2 rr = unpack2<T>(pk[i >> 1]);
+              pr[i >> 1] = pack2<T>(p0 - rr.x, p1 - rr.y);
+            }
+          }
+          tmem_st8(tp + c * 8, pk);  // keys c*16 .. c*16+15
+          if constexpr (kSplitP) tmem_st8(tp + 32 + c * 8, pr);
+        }
+        l += (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        bool late = false;
+        if (j > 0 && !rescale) {
+          late = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((g - 1) & 1), kTcWaitNs);
+          late = __any_sync(0xffffffffu, late);
+        }
+        tc_fence_before();
+        if (group_any(1 + x, late)) {  // P published by all four warps, unless one of them gave up
+          abort = true;
+          break;
+        }
+        if (r == 0) mbar_arrive(&bars[kBarPFull + x]);
+      }
+      if (abort) break;
+      {
+        const bool late = !mbar_wait_bounded(&bars[kBarPv + x], static_cast<uint32_t>((gx + nx - 1) & 1), kTcWaitNs) ||
+                          *s_abort;
+        if (group_any(1 + x, late)) {
+          abort = true;
+          break;
         }
       }
+      tc_fence_after();
+      // Epilogue: O_x / l in two TMEM round trips of 64 columns. Each warp turns its 32 rows
+      // around through its 4 KiB staging tile (16-byte chunk c of row i at chunk c ^ (i & 7): no
+      // bank conflicts either way), so that each global store writes four whole 128-byte row
+      // segments instead of 32 pieces of 16 bytes. Rows past the prompt end are not written.
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int lane = tid & 31;
+      const uint32_t stg = base + LY::kOffE + static_cast<uint32_t>(warp) * 4096u;
+      const int row0 = q0 + x * kTM + (warp & 3) * 32;  // row of lane 0 of this warp
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int qt = 0; qt < 2; ++qt) {
+          float v[32];
+          tmem_ld32(tmem_o(x) + lane_off + half * 64 + qt * 32, v);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const int c = qt * 4 + c4;
+            const uint32_t a = stg + static_cast<uint32_t>(lane) * 128u + static_cast<uint32_t>((c ^ (lane & 7)) * 16);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                         "r"(pack2<T>(v[c4 * 8 + 0] * inv, v[c4 * 8 + 1] * inv)),
+                         "r"(pack2<T>(v[c4 * 8 + 2] * inv, v[c4 * 8 + 3] * inv)),
+                         "r"(pack2<T>(v[c4 * 8 + 4] * inv, v[c4 * 8 + 5] * inv)),
+                         "r"(pack2<T>(v[c4 * 8 + 6] * inv, v[c4 * 8 + 7] * inv))
+                         : "memory");
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3), cc = lane & 7;  // row rr of the warp, chunk cc
+          const uint32_t a = stg + static_cast<uint32_t>(rr) * 128u + static_cast<uint32_t>((cc ^ (rr & 7)) * 16);
+          uint4 w;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w) : "r"(a) : "memory");
+          if (row0 + rr < L)
+            *reinterpret_cast<uint4*>(out + static_cast<int64_t>(s0 + row0 + rr) * o_stride + static_cast<int64_t>(h) * 128 +
+                                      half * 64 + cc * 8) = w;
+        }
+        __syncwarp();
+      }
+      // O_x has been read: the next item's first P V may overwrite it
+      tc_fence_before();
+      group_any(1 + x, false);
+      if (r == 0) mbar_arrive(&bars[kBarOFree + x]);
+      gx += nx;
     }
   }
   if (abort) atomicOr(&g_deverr_prefill, AEG_DEVERR_WAIT_TIMEOUT);
@@ -584,11 +763,18 @@ int launch_prefill_tc(void* out, int64_t o_stride, const void* q, int64_t q_stri
       configured[dev] = true;
     }
   }
-  const dim3 grid(static_cast<unsigned>(Hq), static_cast<unsigned>(B),
-                  static_cast<unsigned>((max_seqlen + 2 * kTM - 1) / (2 * kTM)));
-  prefill_tc_kernel<T><<<grid, kTThreads, TcLayout::kSmem, stream>>>(
-      qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, max_seqlen, Hq / Hkv,
-      static_cast<float>(static_cast<double>(scale) * 1.4426950408889634));
+  static int sm_count[kMaxDevices] = {0};
+  if (sm_count[dev] == 0) AEG_CHECK_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
+  const int levels = (max_seqlen + 2 * kTM - 1) / (2 * kTM);
+  const int64_t items = int64_t(Hq) * B * levels;
+  if (items > int64_t(0x7fffffff))
+    return set_error(AEG_ERR_INVALID_ARGUMENT, "prefill_attention: %lld work items exceed 2^31", (long long)items);
+  static std::atomic<unsigned> launches{0};
+  const int slot = static_cast<int>(launches.fetch_add(1) % kCounterSlots);
+  const unsigned ctas = static_cast<unsigned>(std::min<int64_t>(sm_count[dev], items));
+  prefill_tc_kernel<T><<<ctas, kTThreads, TcLayout::kSmem, stream>>>(
+      qm, km, vm, static_cast<T*>(out), o_stride, cu, num_tokens, B, Hq, levels, max_seqlen, Hq / Hkv,
+      static_cast<float>(static_cast<double>(scale) * 1.4426950408889634), slot);
   AEG_CHECK_LAUNCH("prefill_attention(tcgen05)");
   return AEG_OK;
 }
