@@ -16,9 +16,12 @@
 // a mask-free softmax path for fully visible key tiles (a branch around the warp-collective TMEM
 // loads: 0.414 vs 0.316 ms), one thread issuing every load and MMA with P through shared memory
 // (284 / 328: a refill waited for all MMAs of the previous key tile before the next P was
-// served), and one MMA thread serving both query tiles in the order their P arrive (312 / 360
-// with one thread vs 357 / 409 with one per query tile: issuing a tile's P V and next scores
-// takes that thread 0.5-0.6 us).
+// served), one MMA thread serving both query tiles in the order their P arrive (312 / 360 with
+// one thread vs 357 / 409 with one per query tile: issuing a tile's P V and next scores takes
+// that thread 0.5-0.6 us), one CTA per item (357 / 409 vs 391 / 488 persistent: per CTA ~0.7 us
+// of setup, ~2 us before the first scores and ~1 us between CTAs on an SM), and 16-byte output
+// stores straight from each lane's row (32 rows touched per store instruction: the epilogue took
+// ~2 us, most of it waiting on those stores).
 #include "aeg_common.cuh"
 
 #include <cuda.h>
@@ -43,13 +46,15 @@ __device__ __forceinline__ float ex2p(float x) {
 }
 
 // ---------------------------------------------------------------------------------------
-// tcgen05 kernel. One CTA = 256 query rows of one head of one prompt as two 128-row tiles A and
-// B, each owned by a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row
-// t of its tile = TMEM lane t), an MMA warp (warp 8) whose first thread issues every tcgen05.mma,
-// and a load warp (warp 9) whose first thread issues every TMA load. Keys come in tiles of 64
-// through a 5-stage TMA ring shared by both query tiles; the load thread refills a stage as soon
-// as the MMAs that read it have completed, so the MMA thread never waits on a refill. Per key
-// tile j and query tile X:
+// tcgen05 kernel, persistent: one CTA per SM works through items taken from a per-launch counter.
+// An item is 256 query rows of one head of one prompt as two 128-row tiles A and B, each owned by
+// a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row t of its tile =
+// TMEM lane t); each tile has an MMA warp (warps 8 and 10) whose first thread issues its
+// tcgen05.mma, and a load warp (warp 9) whose first thread fetches items and issues every TMA
+// load. Keys come in tiles of 64 through a 4-stage TMA ring shared by both query tiles and
+// running on across items; the load thread refills a stage as soon as the MMAs that read it have
+// completed, and publishes the next item's record and Q as soon as every warp is done with the
+// current ones. Per key tile j and query tile X:
 //   S_X(j) = Q_X K(j)^T  8 MMAs (M 128, N 64, K 16) into TMEM S_X[j & 1] (64 fp32 columns);
 //   softmax               the warpgroup reads its rows of S_X(j) in one tcgen05.ld, computes
 //                         exp2 / sum, and writes P in the input dtype back over S_X(j) in TMEM
@@ -57,13 +62,13 @@ __device__ __forceinline__ float ex2p(float x) {
 //   O_X += P V(j)          4 MMAs (M 128, N 128, K 16; bf16: 8) into TMEM O_X with A = P read from
 //                         TMEM and B = V read MN-major straight from its TMA layout.
 // MMAs issued by one thread run in issue order, so S_X(j + 2), issued after O_X += P V(j), cannot
-// overwrite P_X(j) before it is read. O never leaves TMEM until the end: a row is rescaled in place
-// (tcgen05.ld / st) only when its running maximum grows by more than 8 in the exp2 domain, so P
-// stays below 2^8, and only then does the softmax wait for the previous P V. While one warpgroup
-// runs its softmax the tensor pipe works on the other tile's MMAs. Every wait is bounded: a
-// timeout is recorded, the CTA stops issuing, drains its own loads (bounded), frees TMEM and
-// returns without writing.
-constexpr int kTM = 128;                 // query rows per tile (two tiles per CTA)
+// overwrite P_X(j) before it is read. O never leaves TMEM until the item's epilogue: a row is
+// rescaled in place (tcgen05.ld / st) only when its running maximum grows by more than 8 in the
+// exp2 domain, so P stays below 2^8, and only then does the softmax wait for the previous P V.
+// While one warpgroup runs its softmax the tensor pipe works on the other tile's MMAs. Every wait
+// is bounded: a timeout is recorded, the CTA stops issuing, drains its own loads and MMAs
+// (bounded), frees TMEM and returns; rows it did not finish are not written.
+constexpr int kTM = 128;                 // query rows per tile (two tiles per item)
 constexpr int kTN = 64;                  // keys per tile
 constexpr int kTThreads = 11 * 32;       // 2 softmax warpgroups, the MMA warps of tiles A and B, the load warp
 constexpr int kQHalf = kTM * 128;        // one SW128 box of Q: 128 rows x 64 elements (16 KiB)

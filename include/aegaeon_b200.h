@@ -237,7 +237,11 @@ AEG_API int aeg_copy_segments(void* dst_base, const void* src_base, const int64_
  *   out[i, h] = softmax_j(scale * q[i, h] . k[j, h / (Hq / Hkv)]) . v[j, h / (Hq / Hkv)], j = 0 .. i
  * fp32 accumulation, output rounded to the input dtype. D = 128. A prompt whose range leaves
  * [0, num_tokens) or exceeds max_seqlen is skipped (its rows are not written) and raises
- * AEG_DEVERR_SEQ_LEN_RANGE. */
+ * AEG_DEVERR_SEQ_LEN_RANGE. The launch is persistent (one CTA per SM) and takes its work from a
+ * device counter, one of 64 the library rotates over per launch (each launch's last CTA resets
+ * its own): launches on several streams may overlap as long as fewer than 64 are in flight at
+ * once; a CUDA graph that holds a launch reuses that launch's counter at every replay, so two
+ * replays of one graph are not run concurrently. */
 AEG_API int aeg_prefill_attention(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                                   const void* k, int64_t k_stride, const void* v, int64_t v_stride,
                                   const int32_t* cu_seqlens, int64_t num_tokens, int B, int max_seqlen,

@@ -63,6 +63,43 @@ def test_prefill_long_prompts_match_torch_fp32(cuda_device, dtype):
         assert bool(((got - ref).abs() <= tol).all()), (b, float((got - ref).abs().max()))
 
 
+def test_prefill_work_counter_repeats_and_streams(cuda_device):
+    """The kernel's CTAs take (level, prompt, head) items from a per-launch counter; the host
+    rotates over 64 counter slots and each launch's last CTA resets its slot. More than 64
+    launches in a row, launches on two streams at once, a batch with fewer items than SMs and a
+    batch of mostly empty prompts must all give the bits of a first, solo launch."""
+    scale = 128 ** -0.5
+    batches = [([300, 1, 777, 64], 28, 4, torch.bfloat16), ([5], 8, 8, torch.float16),
+               ([0, 0, 513, 0, 0, 0, 2], 28, 4, torch.float16)]
+    runs = []
+    for i, (lens, Hq, Hkv, dtype) in enumerate(batches):
+        q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 20 + i)
+        ref = ops.flash_attn_varlen_prefill(q, k, v, cu, max(lens), scale)
+        runs.append((q, k, v, cu, max(lens), ref))
+    torch.cuda.synchronize()
+    for rep in range(70):
+        q, k, v, cu, mx, ref = runs[rep % len(runs)]
+        out = ops.flash_attn_varlen_prefill(q, k, v, cu, mx, scale)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), rep
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+    outs = []
+    for rep in range(12):
+        q, k, v, cu, mx, ref = runs[rep % len(runs)]
+        with torch.cuda.stream(streams[rep % 2]):
+            outs.append((ops.flash_attn_varlen_prefill(q, k, v, cu, mx, scale), ref))
+    torch.cuda.synchronize()
+    for i, (got, ref) in enumerate(outs):
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), i
+    assert ops.read_device_errors(cuda_device) == 0
+    # the mostly-empty batch is still right
+    q, k, v, cu, mx, ref = runs[2]
+    want = orc.np_prefill_attention(_bits(q), _bits(k), _bits(v), cu.cpu().numpy(), scale, orc.FP16)
+    ok, err, excess = orc.compare_attention(_bits(ref), want, orc.FP16)
+    assert ok, (err, excess)
+
+
 def test_prefill_rejects_out_of_range_prompts(cuda_device):
     lens = [10, 20]
     q, k, v, cu = _inputs(cuda_device, lens, 8, 8, torch.float16, 1)
