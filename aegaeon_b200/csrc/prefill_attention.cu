@@ -21,7 +21,9 @@
 // that thread 0.5-0.6 us), one CTA per item (357 / 409 vs 391 / 488 persistent: per CTA ~0.7 us
 // of setup, ~2 us before the first scores and ~1 us between CTAs on an SM), and 16-byte output
 // stores straight from each lane's row (32 rows touched per store instruction: the epilogue took
-// ~2 us, most of it waiting on those stores).
+// ~2 us, most of it waiting on those stores), and 2, 3 or 4 of every 8 exponents taken on the
+// FMA pipe by range reduction and a polynomial instead of ex2 (bf16 / fp16 338 / 432, 335 / 423,
+// 303 / 398 vs 391 / 488: the softmax is bound by instruction issue, not by the ex2 unit).
 #include "aeg_common.cuh"
 
 #include <cuda.h>
@@ -43,6 +45,32 @@ __device__ __forceinline__ float ex2p(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Two fp32 lanes in one instruction (sm_100 packed f32x2): a * b + c, and a + b.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -571,13 +599,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
               sv[i] = (key <= row && key < L) ? sv[i] : -INFINITY;
             }
           }
-          // eight independent partial maxima instead of one 64-long dependent chain
-          float mp[8];
+          // a tree of 3-input maxima: 32 instructions, 4 deep
+          float m1[22], m2[8];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) mp[c] = sv[c];
+          for (int i = 0; i < 21; ++i) m1[i] = max3f(sv[3 * i], sv[3 * i + 1], sv[3 * i + 2]);
+          m1[21] = sv[63];
 #pragma unroll
-          for (int i = 8; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
-          mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+          for (int i = 0; i < 7; ++i) m2[i] = max3f(m1[3 * i], m1[3 * i + 1], m1[3 * i + 2]);
+          m2[7] = m1[21];
+          mx = max3f(max3f(m2[0], m2[1], m2[2]), max3f(m2[3], m2[4], m2[5]), fmaxf(m2[6], m2[7]));
           mx *= scale_log2;
         }
         const bool grow = mx > m_used + kRescaleAbove;
@@ -618,16 +648,17 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           m_used = mx;
         }
         const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-        float rsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+        float2 rsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // independent partial row sums
+        const float2 scale2 = make_float2(scale_log2, scale_log2), base2 = make_float2(neg_base, neg_base);
         const uint32_t tp = tmem_s(x, g & 1) + lane_off;  // P over S: keys 2c, 2c + 1 in column c
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[8], pr[8];
 #pragma unroll
           for (int i = 0; i < 16; i += 2) {
-            const float p0 = ex2p(fmaf(sv[c * 16 + i], scale_log2, neg_base));  // masked keys: ex2(-inf) = 0
-            const float p1 = ex2p(fmaf(sv[c * 16 + i + 1], scale_log2, neg_base));
-            rsum[(i >> 1) & 3] += p0 + p1;
+            const float2 a = fma2(make_float2(sv[c * 16 + i], sv[c * 16 + i + 1]), scale2, base2);
+            const float p0 = ex2p(a.x), p1 = ex2p(a.y);  // masked keys: ex2(-inf) = 0
+            rsum[(i >> 1) & 1] = add2(rsum[(i >> 1) & 1], make_float2(p0, p1));
             pk[i >> 1] = pack2<T>(p0, p1);
             if constexpr (kSplitP) {
               const float2 rr = unpack2<T>(pk[i >> 1]);
@@ -637,7 +668,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           tmem_st8(tp + c * 8, pk);  // keys c*16 .. c*16+15
           if constexpr (kSplitP) tmem_st8(tp + 32 + c * 8, pr);
         }
-        l += (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
+        l += (rsum[0].x + rsum[1].x) + (rsum[0].y + rsum[1].y);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         bool late = false;
         if (j > 0 && !rescale) {
