@@ -21,7 +21,9 @@
 // that thread 0.5-0.6 us), one CTA per item (357 / 409 vs 391 / 488 persistent: per CTA ~0.7 us
 // of setup, ~2 us before the first scores and ~1 us between CTAs on an SM), and 16-byte output
 // stores straight from each lane's row (32 rows touched per store instruction: the epilogue took
-// ~2 us, most of it waiting on those stores), and 2, 3 or 4 of every 8 exponents taken on the
+// ~2 us, most of it waiting on those stores), items of two consecutive row tiles of one head
+// for every head (tile B then needs two more key tiles than A, which waits: 402 / 505 vs 434 /
+// 516 with head pairs), and 2, 3 or 4 of every 8 exponents taken on the
 // FMA pipe by range reduction and a polynomial instead of ex2 (bf16 / fp16 338 / 432, 335 / 423,
 // 303 / 398 vs 391 / 488: the softmax is bound by instruction issue, not by the ex2 unit).
 #include "aeg_common.cuh"
@@ -75,9 +77,10 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
 
 // ---------------------------------------------------------------------------------------
 // tcgen05 kernel, persistent: one CTA per SM works through items taken from a per-launch counter.
-// An item is 256 query rows of one head of one prompt as two 128-row tiles A and B, each owned by
-// a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row t of its tile =
-// TMEM lane t); each tile has an MMA warp (warps 8 and 10) whose first thread issues its
+// An item is two 128-row query tiles A and B of one prompt whose heads share a KV head: the same
+// rows of two query heads (GQA), or, for a lone head, two consecutive row tiles of it. Each tile
+// is owned by a softmax warpgroup (warps 0-3 and 4-7; thread t of a warpgroup owns query row t of
+// its tile = TMEM lane t); each tile has an MMA warp (warps 8 and 10) whose first thread issues its
 // tcgen05.mma, and a load warp (warp 9) whose first thread fetches items and issues every TMA
 // load. Keys come in tiles of 64 through a 4-stage TMA ring shared by both query tiles and
 // running on across items; the load thread refills a stage as soon as the MMAs that read it have
@@ -127,10 +130,11 @@ constexpr int kBarQFull = 0, kBarQFree = 1, kBarKFull = 2, kBarVFull = kBarKFull
               kBarCount = kBarDrain + 2;
 constexpr int kQFreeArrivals = 2 + 8;
 
-// One work item: query tiles A and B (rows q0 .. q0 + 255) of head h of the prompt at s0 of
-// length L, with nA / nB key tiles; nA < 0 marks the end of the work.
+// One work item of the prompt at s0 of length L: query tile A (128 rows from qA of head hA) and
+// query tile B (128 rows from qB of head hB; none when nB = 0), with nA / nB key tiles; both
+// heads read the same KV head. nA < 0 marks the end of the work.
 struct PfItem {
-  int s0, L, h, q0, nA, nB;
+  int s0, L, qA, qB, hA, hB, nA, nB;
 };
 static_assert(8 * kBarCount + 8 + sizeof(PfItem) <= 512,
               "mbarrier slots, the TMEM address, the abort flag and the item record fit the barrier area");
@@ -317,10 +321,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   bool abort = false;
   if (warp == 9) {
     // ------------------------------- work items and loads -------------------------------
-    // Items are (query-tile level, prompt, head), heaviest level first, taken from the launch's
-    // counter. The next item is fetched while the current one computes; its Q and the item
-    // record go out once every warp is done with the current item's (QFree), its key tiles into
-    // the ring as the MMA threads release stages.
+    // The counter runs over (level of 256 query rows, prompt, head slot), heaviest level first;
+    // a (level, prompt) has Hq slots, G per KV head. With G >= 2 a KV head's first 2 * (G / 2)
+    // slots are head pairs (2p, 2p + 1) over the later 128 rows of the level, then over the
+    // earlier 128: both tiles of such an item have the same rows, so they need the same key
+    // tiles and share them. An odd G's last head takes the level's two 128-row tiles as A and B
+    // (B then needs two more key tiles than A), as does every head when G = 1. The next item is
+    // fetched while the current one computes; its Q and the item record go out once every warp is
+    // done with the current item's (QFree), its key tiles into the ring as the MMA threads
+    // release stages.
     if ((tid & 31) == 0) {
       const unsigned per_level = static_cast<unsigned>(B) * static_cast<unsigned>(Hq);
       const unsigned total = per_level * static_cast<unsigned>(levels);
@@ -331,23 +340,34 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           if (i >= total) return;
           const int lv = static_cast<int>(i / per_level);
           const int rem = static_cast<int>(i % per_level);
-          const int b = rem / Hq, h = rem % Hq;
-          const int q0 = (levels - 1 - lv) * 2 * kTM;
+          const int b = rem / Hq, slot_h = rem % Hq;
+          const int lv0 = (levels - 1 - lv) * 2 * kTM;  // first row of the level
           const int s0 = cu_seqlens[b];
           const int L = cu_seqlens[b + 1] - s0;
           const bool valid = s0 >= 0 && L >= 0 && static_cast<int64_t>(s0) + L <= num_tokens && L <= max_seqlen;
           if (!valid) atomicOr(&g_deverr_prefill, AEG_DEVERR_SEQ_LEN_RANGE);
-          if (!valid || L == 0 || q0 >= L) {
-            // every head of this (level, prompt) is empty: move the counter past them
+          if (!valid || L == 0 || lv0 >= L) {
+            // every slot of this (level, prompt) is empty: move the counter past them
             atomicMax(&g_pf_next[slot], static_cast<unsigned>(lv) * per_level + static_cast<unsigned>(b + 1) * Hq);
             continue;
           }
+          const int kvh = slot_h / G, j = slot_h % G, pairs = G / 2;
           it.s0 = s0;
           it.L = L;
-          it.h = h;
-          it.q0 = q0;
-          it.nA = (min(L, q0 + kTM) + kTN - 1) / kTN;
-          it.nB = q0 + kTM < L ? (min(L, q0 + 2 * kTM) + kTN - 1) / kTN : 0;
+          if (j < 2 * pairs) {  // heads (2p, 2p + 1) of the KV head, one 128-row half of the level
+            const int q0 = lv0 + (j < pairs ? kTM : 0);
+            if (q0 >= L) continue;
+            it.qA = it.qB = q0;
+            it.hA = kvh * G + 2 * (j % pairs);
+            it.hB = it.hA + 1;
+            it.nA = it.nB = (min(L, q0 + kTM) + kTN - 1) / kTN;
+          } else {  // the last head of an odd G: the level's two 128-row tiles
+            it.qA = lv0;
+            it.qB = lv0 + kTM;
+            it.hA = it.hB = kvh * G + G - 1;
+            it.nA = (min(L, lv0 + kTM) + kTN - 1) / kTN;
+            it.nB = lv0 + kTM < L ? (min(L, lv0 + 2 * kTM) + kTN - 1) / kTN : 0;
+          }
           return;
         }
       };
@@ -374,8 +394,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         if (!published_end && (k == 0 || mbar_test(&bars[kBarQFree], static_cast<uint32_t>((k - 1) & 1)))) {
           s_item->s0 = nxt.s0;
           s_item->L = nxt.L;
-          s_item->h = nxt.h;
-          s_item->q0 = nxt.q0;
+          s_item->qA = nxt.qA;
+          s_item->qB = nxt.qB;
+          s_item->hA = nxt.hA;
+          s_item->hB = nxt.hB;
           s_item->nA = nxt.nA;
           s_item->nB = nxt.nB;
           if (nxt.nA < 0) {  // no more work: the record alone
@@ -383,15 +405,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             published_end = true;
           } else {
             const PfItem it = nxt;
-            const int n_tiles = it.nB > 0 ? it.nB : it.nA;
+            const int n_tiles = max(it.nA, it.nB);
             mbar_arrive_expect_tx(&bars[kBarQFull], (it.nB > 0 ? 4 : 2) * kQHalf);
-            tma_load_2d(sQx(0), &qmap, bar_u32(kBarQFull), it.h * 128, it.s0 + it.q0);
-            tma_load_2d(sQx(0) + kQHalf, &qmap, bar_u32(kBarQFull), it.h * 128 + 64, it.s0 + it.q0);
+            tma_load_2d(sQx(0), &qmap, bar_u32(kBarQFull), it.hA * 128, it.s0 + it.qA);
+            tma_load_2d(sQx(0) + kQHalf, &qmap, bar_u32(kBarQFull), it.hA * 128 + 64, it.s0 + it.qA);
             if (it.nB > 0) {
-              tma_load_2d(sQx(1), &qmap, bar_u32(kBarQFull), it.h * 128, it.s0 + it.q0 + kTM);
-              tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQFull), it.h * 128 + 64, it.s0 + it.q0 + kTM);
+              tma_load_2d(sQx(1), &qmap, bar_u32(kBarQFull), it.hB * 128, it.s0 + it.qB);
+              tma_load_2d(sQx(1) + kQHalf, &qmap, bar_u32(kBarQFull), it.hB * 128 + 64, it.s0 + it.qB);
             }
-            (n_pend == 0 ? p0 : p1) = Pending{t_end, n_tiles, it.s0, it.h / G};
+            (n_pend == 0 ? p0 : p1) = Pending{t_end, n_tiles, it.s0, it.hA / G};
             ++n_pend;
             t_end += n_tiles;
             ++k;
@@ -491,7 +513,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         if (nA < 0) break;
         const int nx = x == 0 ? nA : nB;
         const int n_other = x == 0 ? nB : nA;
-        const int n_tiles = nB > 0 ? nB : nA;
+        const int n_tiles = max(nA, nB);
         if (nx == 0) {  // no tile x in this item
           mbar_arrive(&bars[kBarQFree]);
           t_base += n_tiles;
@@ -568,14 +590,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         abort = true;
         break;
       }
-      const int s0 = s_item->s0, L = s_item->L, h = s_item->h, q0 = s_item->q0;
+      const int s0 = s_item->s0, L = s_item->L;
+      const int q0 = x == 0 ? s_item->qA : s_item->qB, h = x == 0 ? s_item->hA : s_item->hB;  // this tile's
       const int nA = s_item->nA, nB = s_item->nB;
       __syncwarp();
       if ((tid & 31) == 0) mbar_arrive(&bars[kBarQFree]);  // this warp has read the item record
       if (nA < 0) break;
       const int nx = x == 0 ? nA : nB;
       if (nx == 0) continue;
-      const int row = q0 + x * kTM + r;
+      const int row = q0 + r;
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < nx; ++j) {
         const int g = gx + j;
@@ -592,7 +615,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         if (!bad) {
           tc_fence_after();
           tmem_ld64(tmem_s(x, g & 1) + lane_off, sv);
-          if (!(key0 + kTN - 1 <= q0 + x * kTM && key0 + kTN <= L)) {
+          if (!(key0 + kTN - 1 <= q0 && key0 + kTN <= L)) {
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
               const int key = key0 + i;
@@ -699,7 +722,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int lane = tid & 31;
       const uint32_t stg = base + LY::kOffE + static_cast<uint32_t>(warp) * 4096u;
-      const int row0 = q0 + x * kTM + (warp & 3) * 32;  // row of lane 0 of this warp
+      const int row0 = q0 + (warp & 3) * 32;  // row of lane 0 of this warp
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
 #pragma unroll

@@ -30,7 +30,7 @@ def _inputs(dev, lens, Hq, Hkv, dtype, seed):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (8, 8)])
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (8, 8), (16, 4), (12, 4)])
 def test_prefill_matches_oracle(cuda_device, dtype, Hq, Hkv):
     lens = [1, 17, 64, 65, 0, 130]
     q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 3)
