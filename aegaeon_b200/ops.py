@@ -554,6 +554,16 @@ class DecodePlan:
         self.block_tables = block_tables
         return self
 
+    def stats(self) -> dict:
+        """What the last ``plan`` built, read back from the workspace header (waits for the plan):
+        the cost-axis positions (blocks plus kUnitCost per non-empty (sequence, head) pair), the
+        worker warps the positions were cut for, the units (pieces of pairs between pair ends and
+        warp starts), the split-pair entries (pairs cut across warps, plus empty pairs), the
+        partial-result slots those pieces write, and the split-merge items."""
+        words = self.workspace[:24].view(torch.int32).cpu().tolist()
+        keys = ("items", "workers", "units", "split_pair_entries", "partial_slots", "merge_items")
+        return dict(zip(keys, words))
+
     def matches(self, B: int, Hq: int, Hkv: int, D: int, block_table: torch.Tensor, seq_lens: torch.Tensor) -> bool:
         return ((self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim) == (B, Hq, Hkv, D)
                 and self.block_tables is not None and self.block_tables.data_ptr() == block_table.data_ptr()

@@ -849,6 +849,7 @@ def run_decode(args, world, rank, local):
                                  "launch alone (reshape_and_cache_isolated_us)",
             "reshape_and_cache_isolated_us": statistics.median(write_ms) * 1e3,
             "plan_median_us": plan_med_ms * 1e3,
+            "plan": step.plan.stats(),
         },
         "clocks": clock_info,
     }

@@ -233,3 +233,24 @@ def test_matches_vllm_golden_vectors(cuda_device, name):
     got = out.view(torch.int16).cpu().numpy().view(np.uint16)
     ok, err, excess = orc.compare_attention(got, g["out_vllm"], orc.BF16 if dt == torch.bfloat16 else orc.FP16)
     assert ok, (err, excess)
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg3"])
+def test_plan_stats_describe_the_batch(cuda_device, name):
+    """DecodePlan.stats() reads back what the plan built; its counts follow from the batch: one
+    position per (sequence, head) block plus the start cost of every non-empty pair, at least one
+    unit per non-empty pair, one more per warp start inside a pair, and two partial slots per
+    such cut at most."""
+    cfg = synth.CONFIGS[name]
+    lay = synth.make_layout(cfg)
+    plan = ops.DecodePlan(cfg.batch, cfg.num_q_heads, cfg.num_kv_heads, 128, cuda_device)
+    plan.plan(torch.as_tensor(lay.seq_lens, device=cuda_device), torch.as_tensor(lay.block_tables, device=cuda_device))
+    st = plan.stats()
+    nb = (np.asarray(lay.seq_lens, dtype=np.int64) + 15) // 16
+    nonempty = int((nb > 0).sum()) * cfg.num_kv_heads
+    assert st["items"] == int(nb.sum()) * cfg.num_kv_heads + 2 * nonempty
+    assert nonempty <= st["units"] <= nonempty + st["workers"]
+    assert st["workers"] % 8 == 0 and st["workers"] > 0
+    assert 0 <= st["partial_slots"] <= 2 * st["workers"]
+    assert st["split_pair_entries"] <= cfg.batch * cfg.num_kv_heads
+    assert st["merge_items"] >= st["split_pair_entries"] - (cfg.batch * cfg.num_kv_heads - nonempty)
