@@ -13,7 +13,8 @@ One JSON line on rank 0 with the step throughput, the dominant kernel's roofline
 an isolated launch, and after a QKV-shaped GEMM as in the model's forward), the end-to-end number
 through the public step API, the host link (one GPU and all ranks at once), the cfg5 KV-block swap
 set beside the reference's own swap operator built from its sources, a cross-GPU migration check
-(N >= 2) and the fp32 torch CPU baseline.
+(N >= 2), the fp32 torch CPU baseline and, at N = 1, the per-layer figures of the other decode
+configurations (cfg1, cfg2, cfg4) on the same GPU.
 
 ``--impl reference`` times the reference path's CPU restatement (oracle/torch_ref.py, fp32 torch,
 all host threads) on whole L-layer steps of a bounded sample of the same workload, with the same
@@ -53,6 +54,8 @@ def _args():
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-swap", action="store_true", help="decode configs: skip the swap-set leg")
+    p.add_argument("--no-other-configs", action="store_true",
+                   help="cfg3 at N = 1: skip the per-layer figures of cfg1, cfg2 and cfg4")
     p.add_argument("--swap-scale", type=float, default=1.0, help="decode configs: scale the swap set (small cases)")
     p.add_argument("--unfused", action="store_true",
                    help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
@@ -597,6 +600,73 @@ def migration_leg(kv: torch.Tensor, world: int, rank: int, device, n_blocks: int
                    "SM kernel, plain peer loads), all ranks at once; bit-exact by digests of source and target"}
 
 
+def other_configs_leg(device, peak: float, max_layers: int = 4) -> dict:
+    """cfg1, cfg2 and cfg4, the other decode configurations, beside the cfg3 headline on the same
+    GPU: each as a step graph (plan + fused cache write and attention per layer) of its layers, at
+    most ``max_layers`` of them for cfg4 (its pool then holds those layers only: same blocks and
+    bytes per launch), per layer = (step - plan) / layers, and as launches timed alone. Tokens/s
+    of a whole step follow as batch / (plan + layers x per-layer time)."""
+    from aegaeon_b200 import ops, synth
+    from aegaeon_b200.step import DecodeStep
+
+    res = {}
+    for name in ("cfg1", "cfg2", "cfg4"):
+        cfg = synth.CONFIGS[name]
+        lt = min(cfg.num_layers, max_layers) if name == "cfg4" else cfg.num_layers
+        cfg_t = dataclasses.replace(cfg, num_layers=lt)
+        lay = synth.make_layout(cfg_t)
+        B = len(lay.seq_lens)
+        Hq, Hkv, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+        scale = synth.default_scale(cfg)
+        kv = torch.empty((lay.num_blocks, lt, 2, 16, Hkv, D), dtype=cfg.dtype, device=device)
+        synth.fill_normal_(kv, cfg.value_std, cfg.seed)
+        step = DecodeStep(kv, Hq, B, lay.width, scale)
+        g = torch.Generator(device=device).manual_seed(cfg.seed + 17)
+        step.load_inputs(q=(torch.randn(step.q.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                         k_new=(torch.randn(step.k_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                         v_new=(torch.randn(step.v_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                         slot_mapping=torch.as_tensor(synth.new_token_slots(lay), device=device),
+                         block_tables=torch.as_tensor(lay.block_tables, device=device),
+                         seq_lens=torch.as_tensor(lay.seq_lens, device=device))
+        step.capture()
+        for _ in range(3):
+            step.replay()
+        stream = torch.cuda.current_stream(device)
+        reps = 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        a.record(stream)
+        for _ in range(reps):
+            step.replay()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        step_ms = a.elapsed_time(b) / reps
+        assert torch.isfinite(step.out.float()).all(), f"non-finite {name} output"
+        plan_ms = statistics.median(_per_launch_ms([lambda: step.plan.plan(step.seq_lens, step.block_tables)] * 4,
+                                                   device))
+        fns = [lambda l=l: ops.decode_layer(step.out[l], step.q[l], step.k_new[l], step.v_new[l], kv, l,
+                                            step.block_tables, step.seq_lens, scale, plan=step.plan)
+               for l in range(lt)]
+        iso_ms = statistics.median(_per_launch_ms(fns * max(1, 8 // lt), device))
+        algo = synth.algorithmic_bytes_per_layer(cfg_t, lay)
+        lb = algo["attention"] + algo["reshape_and_cache"]
+        per_layer = max((step_ms - plan_ms) / lt, 1e-6)
+        res[name] = {
+            "workload": f"{name}: {Hq}/{Hkv} heads, {str(cfg.dtype).replace('torch.', '')}, batch {B}, "
+                        f"{_ctx_desc(cfg)}, {lt} of {cfg.num_layers} layers in the step graph",
+            "layer_bytes": lb,
+            "in_step_launch_us": per_layer * 1e3,
+            "frac": lb / (per_layer / 1e3) / 1e9 / peak,
+            "isolated_launch_us": iso_ms * 1e3,
+            "frac_isolated_launch": lb / (iso_ms / 1e3) / 1e9 / peak,
+            "plan_us": plan_ms * 1e3,
+            "tokens_per_s": B / ((plan_ms + per_layer * cfg.num_layers) / 1e3),
+        }
+        del step, kv
+        torch.cuda.empty_cache()
+    return res
+
+
 def run_decode(args, world, rank, local):
     from aegaeon_b200 import ops, synth
     from aegaeon_b200.step import DecodePipeline, DecodeStep
@@ -764,6 +834,9 @@ def run_decode(args, world, rank, local):
     migration = migration_leg(kv, world, rank, device) if world > 1 else None
 
     peak, peak_src = _peaks()
+    others = None
+    if world == 1 and rank == 0 and args.config == "cfg3" and not args.no_other_configs and not args.layers:
+        others = other_configs_leg(device, peak)
     algo = synth.algorithmic_bytes_per_layer(cfg, lay)
     launch_bytes = algo["attention"] + (algo["reshape_and_cache"] if step.fused else 0)
     ms_step = ms / args.steps
@@ -867,6 +940,8 @@ def run_decode(args, world, rank, local):
                                        "d2h": d2h / e2e_step_s / 1e9 / link["d2h_gbs_one_gpu"]}
     if swap is not None:
         line["swap"] = swap
+    if others is not None:
+        line["other_configs"] = others
     if migration is not None:
         line["migration"] = migration
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
