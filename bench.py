@@ -14,7 +14,8 @@ an isolated launch, and after a QKV-shaped GEMM as in the model's forward), the 
 through the public step API, the host link (one GPU and all ranks at once), the cfg5 KV-block swap
 set beside the reference's own swap operator built from its sources, a cross-GPU migration check
 (N >= 2), the fp32 torch CPU baseline and, at N = 1, the per-layer figures of the other decode
-configurations (cfg1, cfg2, cfg4) on the same GPU.
+configurations (cfg1, cfg2, cfg4) and compact figures of the prefill, step-input and weight-switch
+rows (each also a --config of its own) on the same GPU.
 
 ``--impl reference`` times the reference path's CPU restatement (oracle/torch_ref.py, fp32 torch,
 all host threads) on whole L-layer steps of a bounded sample of the same workload, with the same
@@ -55,7 +56,8 @@ def _args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-swap", action="store_true", help="decode configs: skip the swap-set leg")
     p.add_argument("--no-other-configs", action="store_true",
-                   help="cfg3 at N = 1: skip the per-layer figures of cfg1, cfg2 and cfg4")
+                   help="cfg3 at N = 1: skip the per-layer figures of cfg1, cfg2 and cfg4 and the prefill, "
+                        "step-input and weight-switch figures")
     p.add_argument("--swap-scale", type=float, default=1.0, help="decode configs: scale the swap set (small cases)")
     p.add_argument("--unfused", action="store_true",
                    help="run each layer as reshape_and_cache + paged_attention_decode (two operators)")
@@ -667,6 +669,28 @@ def other_configs_leg(device, peak: float, max_layers: int = 4) -> dict:
     return res
 
 
+def rows_leg(local) -> dict:
+    """The other rows' own measurements (their --config runs) in compact form for the default line
+    at N = 1: prefill attention beside vLLM's FlashAttention, the per-step input builder beside the
+    reference's loops, and the model-weight switch beside the host link and the reference's loop."""
+    ns = argparse.Namespace(steps=20, warmup=3, scale=1.0)
+    pf = prefill_line(ns, local)
+    pr = prep_line(ns, local)
+    ws = run_weights(ns, 1, 0, local, embed=True)
+    return {
+        "prefill": {"metric": pf["metric"], "value": pf["value"], "unit": pf["unit"],
+                    "workload": pf["config"]["workload"], "detail": pf["detail"], "roofline": pf["roofline"],
+                    "cpu_baseline": pf["cpu_baseline"]},
+        "step_inputs": {"metric": pr["metric"], "value": pr["value"], "unit": pr["unit"],
+                        "workload": pr["config"]["workload"], "batches": pr["batches"],
+                        "cpu_baseline": pr["cpu_baseline"]},
+        "weight_switch": {"metric": ws["metric"], "value": ws["value"], "unit": ws["unit"],
+                          "workload": ws["config"]["workload"], "detail_gbs": ws["detail_gbs"],
+                          "roofline": ws["roofline"], "cpu_baseline": ws["cpu_baseline"],
+                          "first_mib_matches": ws["first_mib_matches"]},
+    }
+
+
 def run_decode(args, world, rank, local):
     from aegaeon_b200 import ops, synth
     from aegaeon_b200.step import DecodePipeline, DecodeStep
@@ -834,9 +858,10 @@ def run_decode(args, world, rank, local):
     migration = migration_leg(kv, world, rank, device) if world > 1 else None
 
     peak, peak_src = _peaks()
-    others = None
+    others = rows = None
     if world == 1 and rank == 0 and args.config == "cfg3" and not args.no_other_configs and not args.layers:
         others = other_configs_leg(device, peak)
+        rows = rows_leg(local)
     algo = synth.algorithmic_bytes_per_layer(cfg, lay)
     launch_bytes = algo["attention"] + (algo["reshape_and_cache"] if step.fused else 0)
     ms_step = ms / args.steps
@@ -942,6 +967,8 @@ def run_decode(args, world, rank, local):
         line["swap"] = swap
     if others is not None:
         line["other_configs"] = others
+    if rows is not None:
+        line["rows"] = rows
     if migration is not None:
         line["migration"] = migration
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -1099,7 +1126,7 @@ def _reference_weight_loop(arena, cache, offs, sizes):
         arena[o:o + n].copy_(cache[o:o + n], non_blocking=True)
 
 
-def run_weights(args, world, rank, local, reference_only=False):
+def run_weights(args, world, rank, local, reference_only=False, embed=False):
     """Model-weight switch (GB/s): Qwen2.5-7B's parameters (bf16) from a page-locked host model
     cache into a device arena, one call (copy engines over runs of adjacent parameters, or one
     kernel through the mapped host memory), against the reference's per-parameter copy_ loop
@@ -1137,7 +1164,8 @@ def run_weights(args, world, rank, local, reference_only=False):
     ok = torch.equal(arena[: 1 << 20].cpu(), cache[: 1 << 20])
     gbs = {k.replace("_ms", "_gbs"): (big if k.startswith("link") else total) / (v / 1e3) / 1e9 for k, v in res.items()}
     best = max(gbs["dma_gbs"], gbs["sm_gbs"])
-    print(json.dumps({
+    del arena, cache
+    line = {
         "metric": "weight-switch GB/s", "value": best, "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": 1,
         "ms_per_step": min(res["dma_ms"], res["sm_ms"]), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic parameter bytes", "config": {"workload": workload},
@@ -1147,7 +1175,10 @@ def run_weights(args, world, rank, local, reference_only=False):
                      "peak_source": "measured here: one contiguous 1 GiB pinned host-to-device copy"},
         "cpu_baseline": {"value": gbs["reference_loop_gbs"], "unit": "GB/s", "cores": 1, "kind": "reference",
                          "sample": "the reference's per-parameter copy_ loop (torch), whole model"},
-    }), flush=True)
+    }
+    if embed:
+        return line
+    print(json.dumps(line), flush=True)
 
 
 def _prefill_lengths(scale: float = 1.0):
@@ -1168,6 +1199,10 @@ def _vllm_varlen():
 
 
 def run_prefill(args, world, rank, local):
+    print(json.dumps(prefill_line(args, local)), flush=True)
+
+
+def prefill_line(args, local) -> dict:
     """Prefill attention (TFLOP/s, causal FLOPs 2 x 2 x Hq x D x L(L+1)/2 per prompt): this
     library's kernel on a batch of prompts with inputs resident, beside vLLM's FlashAttention
     varlen kernel on the same inputs when it loads, and the oracle on one prompt of the batch."""
@@ -1224,7 +1259,7 @@ def run_prefill(args, world, rank, local):
     cpu_s = time.perf_counter() - t0
     cpu_tf = 4.0 * Hq * D * Ls * (Ls + 1) / 2 / cpu_s / 1e12
     b = res["bf16"]
-    print(json.dumps({
+    return {
         "metric": "prefill-attn TFLOP/s", "value": b["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": reps,
         "warmup": 1, "ms_per_step": b["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic N(0,1) q/k/v",
@@ -1237,7 +1272,7 @@ def run_prefill(args, world, rank, local):
                      "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"},
         "cpu_baseline": {"value": cpu_tf, "unit": "TFLOP/s", "cores": 1, "kind": "port",
                          "sample": f"the oracle (numpy fp64) on one {Ls}-token prompt, all 28 heads"},
-    }), flush=True)
+    }
 
 
 def _prep_batches():
@@ -1266,6 +1301,12 @@ def _prep_batches():
 
 
 def run_prep(args, world, rank, local):
+    line = prep_line(args, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def prep_line(args, local) -> dict:
     """Per-step model inputs on the device (ops.prepare_step_inputs) against the reference's
     per-request Python loops restated in the oracle (Worker._prepare_model_inputs,
     aegaeon/aegaeon/worker.py:596-682), per batch: device microseconds per step (CUDA events,
@@ -1308,9 +1349,8 @@ def run_prep(args, world, rank, local):
             n_host += 1
         host_us = (time.perf_counter() - t0) / n_host * 1e6
         rows[name] = {"tokens": T, "device_us": dev_us, "host_loop_us": host_us, "matches_oracle": ok}
-    if rank == 0:
-        first = rows[next(iter(rows))]
-        print(json.dumps({
+    first = rows[next(iter(rows))]
+    return {
             "metric": "step-input prep us", "value": first["device_us"], "unit": "us", "n_gpus": 1, "steps": 200,
             "warmup": max(args.warmup, 3), "ms_per_step": first["device_us"] / 1e3, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "int32/int64", "data": "synthetic (bench configs)",
@@ -1320,7 +1360,7 @@ def run_prep(args, world, rank, local):
             "cpu_baseline": {"value": first["host_loop_us"], "unit": "us", "cores": 1, "kind": "port",
                              "sample": "the oracle's restatement of the reference's per-request Python loops "
                                        "(no tensor creation or host-to-device copies), timed for 1 s"},
-        }), flush=True)
+    }
 
 
 # ------------------------------------------------------------------------------------------
