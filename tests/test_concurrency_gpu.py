@@ -28,11 +28,15 @@ SLEEP_CYCLES = int(4e8)  # ~0.2 s of device time at B200 clocks
 
 
 def _warm_kernels(device):
-    """Runs once every kernel the ordering checks launch, so that no lazy module load (which waits
-    for the device) happens while the swap stream is busy."""
+    """Runs once every kernel the ordering checks launch (on scratch pools of their own), so that
+    no lazy module load (which waits for the device) happens while the swap stream is busy."""
     torch.cuda._sleep(1000)
     marker = torch.ones(1, device=device)
     marker += 1
+    dev, host = _pools(2, 2, seed=1)
+    ids = torch.as_tensor([0], device=device)
+    ops.swap_sm(ids, ids, False, dev, host)
+    ops.swap_sm(ids, ids, True, dev, host)
     torch.cuda.synchronize()
 
 
