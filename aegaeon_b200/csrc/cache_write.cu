@@ -4,9 +4,15 @@
 // (aegaeon/aegaeon/worker.py:517-523; slots from worker.py:628-633): slot s maps to block
 // s / 16, row s % 16 of the (16, Hkv, D) block interior; s < 0 is padding and is skipped.
 //
-// One CTA handles one token: its threads move the token's Hkv*D key and value elements as
-// 16-byte vectors (64 + 64 vectors for Hkv=4, D=128). The copy is bit-exact.
+// A decode step's few tokens: one CTA per token, its threads moving the token's Hkv*D key and
+// value elements as 16-byte vectors (64 + 64 vectors for Hkv=4, D=128). A prompt batch's many
+// tokens: one warp per token over a grid of a few CTAs per SM, each lane loading all of its
+// vectors of the token before storing any, so that every resident warp keeps its token's rows in
+// flight (one CTA per token leaves the GPU launching CTAs, with ~5 MB in flight). The copy is
+// bit-exact either way.
 #include "aeg_common.cuh"
+
+#include <algorithm>
 
 namespace aeg {
 namespace {
@@ -14,6 +20,8 @@ namespace {
 __device__ unsigned int g_deverr_cache = 0;
 
 constexpr int kCacheThreads = 128;
+constexpr int kWarpKernelThreads = 256;
+constexpr int64_t kWarpKernelMinTokens = 1024;  // from this many tokens on, one warp per token
 
 // Both kernels run under programmatic dependent launch: they wait for the preceding kernel
 // (which may have produced the keys, values or slots) and then let the next kernel launch, so
@@ -50,6 +58,46 @@ reshape_and_cache_vec_kernel(const uint4* __restrict__ key, const uint4* __restr
       k_cache[dst + i] = key[t * key_stride_v + i];
     else
       v_cache[dst + i - row_vecs] = value[t * value_stride_v + i - row_vecs];
+  }
+}
+
+// Many tokens: warp w takes tokens w, w + warps, ...; its lanes load up to 4 vectors each of the
+// token's K and V rows, then store them.
+__global__ void __launch_bounds__(kWarpKernelThreads)
+reshape_and_cache_warp_kernel(const uint4* __restrict__ key, const uint4* __restrict__ value, int64_t key_stride_v,
+                              int64_t value_stride_v, uint4* __restrict__ k_cache, uint4* __restrict__ v_cache,
+                              int64_t block_stride_v, int64_t num_slots, const int64_t* __restrict__ slot_mapping,
+                              int row_vecs, int64_t T) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kWarpKernelThreads / 32);
+  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * kWarpKernelThreads + threadIdx.x) >> 5; t < T; t += warps) {
+    const int64_t slot = slot_mapping[t];
+    if (slot >= num_slots && lane == 0) atomicOr(&g_deverr_cache, AEG_DEVERR_SLOT_RANGE);
+    const bool write = slot >= 0 && slot < num_slots;
+    const int64_t dst = (slot >> 4) * block_stride_v + (slot & 15) * row_vecs;
+    for (int i0 = lane; i0 < 2 * row_vecs; i0 += 4 * 32) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u;
+        if (i < row_vecs)
+          r[u] = key[t * key_stride_v + i];
+        else if (i < 2 * row_vecs)
+          r[u] = value[t * value_stride_v + i - row_vecs];
+      }
+      if (write) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = i0 + 32 * u;
+          if (i < row_vecs)
+            k_cache[dst + i] = r[u];
+          else if (i < 2 * row_vecs)
+            v_cache[dst + i - row_vecs] = r[u];
+        }
+      }
+    }
   }
 }
 
@@ -116,7 +164,18 @@ extern "C" int aeg_reshape_and_cache(const void* key, const void* value, int64_t
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (vec) {
+  if (vec && T >= aeg::kWarpKernelMinTokens) {
+    int dev = 0, sms = 0;
+    AEG_CHECK_CUDA(cudaGetDevice(&dev));
+    AEG_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t per_cta = aeg::kWarpKernelThreads / 32;
+    cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((T + per_cta - 1) / per_cta, int64_t(sms) * 8)));
+    cfg.blockDim = dim3(aeg::kWarpKernelThreads);
+    AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, aeg::reshape_and_cache_warp_kernel, static_cast<const uint4*>(key),
+                                      static_cast<const uint4*>(value), key_stride / 8, value_stride / 8,
+                                      static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), block_stride / 8,
+                                      num_slots, slot_mapping, static_cast<int>(row / 8), T));
+  } else if (vec) {
     AEG_CHECK_CUDA(cudaLaunchKernelEx(&cfg, aeg::reshape_and_cache_vec_kernel, static_cast<const uint4*>(key),
                                       static_cast<const uint4*>(value), key_stride / 8, value_stride / 8,
                                       static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), block_stride / 8,

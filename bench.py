@@ -1250,6 +1250,36 @@ def prefill_line(args, local) -> dict:
                 res[name]["max_abs_diff_vs_vllm_fa"] = float((ref_out.float() - out.float()).abs().max())
             except Exception as e:  # noqa: BLE001
                 res[name]["vllm_fa"] = f"failed: {type(e).__name__}: {str(e)[:160]}"
+    # The prompt half of the cache write: every prompt token's K and V (bf16) into the blocks of
+    # a 28-layer cache whose prompts own scattered blocks, layer 0 (vLLM's reshape_and_cache_flash
+    # over the prompt tokens). Bytes: K and V read once and written once, plus the slots.
+    nblk = int(sum((int(L) + 15) // 16 for L in lens))
+    pool_blocks = max(4 * nblk, 1024)
+    kv_pool = torch.zeros((pool_blocks, 28, 2, 16, Hkv, D), dtype=torch.bfloat16, device=device)
+    perm = np.random.default_rng(5).permutation(pool_blocks)[:nblk]
+    slots, b0 = [], 0
+    for L in lens:  # each prompt's tokens fill its own blocks in order
+        nb = (int(L) + 15) // 16
+        blocks = perm[b0:b0 + nb]
+        b0 += nb
+        pos = np.arange(int(L))
+        slots.append(blocks[pos // 16] * 16 + pos % 16)
+    slot_t = torch.as_tensor(np.concatenate(slots).astype(np.int64), device=device)
+    # Six input sets (more than L2 together) and a different layer per launch, so that no launch
+    # finds its rows in L2; each launch timed alone between events (launches queued behind a sleep).
+    g = torch.Generator(device=device).manual_seed(12)
+    kns = [torch.randn((T, Hkv, D), generator=g, device=device).to(torch.bfloat16) for _ in range(6)]
+    vns = [torch.randn((T, Hkv, D), generator=g, device=device).to(torch.bfloat16) for _ in range(6)]
+    w_fns = [lambda l=l: ops.reshape_and_cache(kns[l % 6], vns[l % 6], kv_pool, l, slot_t) for l in range(13)]
+    w_ms = statistics.median(_per_launch_ms(w_fns, device)[1:])
+    w_bytes = 2 * 2 * T * Hkv * D * 2 + T * 8
+    res["prompt_cache_write"] = {"tokens": T, "us": w_ms * 1e3, "gbs": w_bytes / (w_ms / 1e3) / 1e9,
+                                 "frac_of_hbm": w_bytes / (w_ms / 1e3) / 1e9 / peak,
+                                 "bytes": w_bytes, "what": "bf16 K/V of every prompt token into scattered blocks "
+                                                           "of one layer of a 28-layer cache; median launch alone "
+                                                           "between events, inputs and layers rotated past L2"}
+    del kns, vns
+    del kv_pool
     # CPU baseline: the oracle (numpy, fp64) on the batch's shortest prompt of at least 256 tokens
     Ls = int(min([L for L in lens if L >= 256] or [int(lens.min())]))
     rng = np.random.default_rng(0)

@@ -136,3 +136,28 @@ def test_prompt_cache_write_bit_exact(cuda_device):
     ref = kv.numpy().view(np.uint16).copy()
     orc.np_reshape_and_cache(key.numpy().view(np.uint16), val.numpy().view(np.uint16), ref[:, 1, 0], ref[:, 1, 1], slots)
     assert np.array_equal(_bits(kv_dev), ref)
+
+
+@pytest.mark.parametrize("Hkv", [4, 40])
+def test_prompt_cache_write_many_tokens(cuda_device, Hkv):
+    """From 1024 tokens on the cache write runs one warp per token: bit-exact against the oracle
+    with padding slots (-1) skipped and an out-of-range slot skipped and reported."""
+    rng = np.random.default_rng(10 + Hkv)
+    T, N, L = 2600, 256, 2
+    slots = rng.permutation(N * 16)[:T].astype(np.int64)
+    slots[::97] = -1
+    slots[5] = N * 16 + 3  # past the pool
+    kv = torch.randint(-32768, 32768, (N, L, 2, 16, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    key = torch.randint(-32768, 32768, (T, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    val = torch.randint(-32768, 32768, (T, Hkv, 128), dtype=torch.int32).to(torch.int16)
+    kv_dev = kv.to(cuda_device).view(torch.float16)
+    ops.read_device_errors(cuda_device)
+    ops.reshape_and_cache(key.to(cuda_device).view(torch.float16), val.to(cuda_device).view(torch.float16), kv_dev,
+                          0, torch.as_tensor(slots, device=cuda_device))
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) & 0x2  # AEG_DEVERR_SLOT_RANGE
+    ok = slots.copy()
+    ok[ok >= N * 16] = -1
+    ref = kv.numpy().view(np.uint16).copy()
+    orc.np_reshape_and_cache(key.numpy().view(np.uint16), val.numpy().view(np.uint16), ref[:, 0, 0], ref[:, 0, 1], ok)
+    assert np.array_equal(_bits(kv_dev), ref)
