@@ -1670,10 +1670,11 @@ int decode_common(void* out, int64_t out_stride, const void* q, int64_t q_stride
 //     AEG_ERR_INVALID_ARGUMENT before anything is enqueued.
 //   * Nothing in the scratch has to start at zero for the first call: the plan kernel that
 //     every call enqueues rewrites the header, the warp, unit, split-pair and merge records,
-//     and sets every CTA's publication flag to zero. The attention kernel then stamps each
-//     CTA's flag with (its value at launch) + 1 once that CTA's partials are stored, and the
-//     merge waits for that stamp; the partial rows are written before they are read. (Static
-//     device memory also starts zeroed when the module is loaded.)
+//     and sets every worker warp's publication flag to zero. The attention kernel then stamps
+//     each worker warp's flag with (its value at launch) + 1 once that warp's partials are
+//     stored, and a merge item waits for that stamp from each warp that computed a piece of its
+//     pair; the partial rows are written before they are read. (Static device memory also
+//     starts zeroed when the module is loaded.)
 //   * A call that fails a check (arguments, sizes, alignment, tensor-map encoding) returns its
 //     error before enqueuing anything, so it leaves the scratch as the previous call left it.
 //   * One scratch per device means calls on one device must not overlap: two calls in flight

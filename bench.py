@@ -1272,12 +1272,22 @@ def prefill_line(args, local) -> dict:
     vns = [torch.randn((T, Hkv, D), generator=g, device=device).to(torch.bfloat16) for _ in range(6)]
     w_fns = [lambda l=l: ops.reshape_and_cache(kns[l % 6], vns[l % 6], kv_pool, l, slot_t) for l in range(13)]
     w_ms = statistics.median(_per_launch_ms(w_fns, device)[1:])
+
+    def w_all():
+        for fn in w_fns:
+            fn()
+
+    w_graph_ms = _graph_ms(w_all, 5, device) / len(w_fns)
     w_bytes = 2 * 2 * T * Hkv * D * 2 + T * 8
     res["prompt_cache_write"] = {"tokens": T, "us": w_ms * 1e3, "gbs": w_bytes / (w_ms / 1e3) / 1e9,
                                  "frac_of_hbm": w_bytes / (w_ms / 1e3) / 1e9 / peak,
+                                 "graph_us": w_graph_ms * 1e3,
+                                 "graph_frac_of_hbm": w_bytes / (w_graph_ms / 1e3) / 1e9 / peak,
                                  "bytes": w_bytes, "what": "bf16 K/V of every prompt token into scattered blocks "
-                                                           "of one layer of a 28-layer cache; median launch alone "
-                                                           "between events, inputs and layers rotated past L2"}
+                                                           "of one layer of a 28-layer cache, inputs and layers "
+                                                           "rotated past L2; us: median launch alone between events; "
+                                                           "graph_us: per launch in a CUDA graph of 13 back-to-back "
+                                                           "launches"}
     del kns, vns
     del kv_pool
     # CPU baseline: the oracle (numpy, fp64) on the batch's shortest prompt of at least 256 tokens
