@@ -36,6 +36,14 @@ def _require_cuda(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be a CUDA tensor")
 
 
+def _same_device(dev: torch.device, **tensors) -> None:
+    """Raises ValueError unless every given tensor lives on ``dev`` (the device the work runs on):
+    a kernel handed another GPU's address would read across NVLink or fault."""
+    for name, t in tensors.items():
+        if t is not None and t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, the operation runs on {dev}")
+
+
 def _ids_array(ids, name: str) -> np.ndarray:
     if isinstance(ids, torch.Tensor):
         ids = ids.detach().cpu().numpy()
@@ -303,6 +311,7 @@ def flash_attn_varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or out.stride(1) != D:
         raise ValueError("out must match q")
     dev = q.device
+    _same_device(dev, k=k, v=v, cu_seqlens=cu_seqlens, out=out)
     with torch.cuda.device(dev):
         st = lib.aeg_prefill_attention(out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(),
                                        k.stride(0), v.data_ptr(), v.stride(0), cu_seqlens.data_ptr(), T,
@@ -406,8 +415,10 @@ def prepare_step_inputs(block_tables: torch.Tensor, context_lens: torch.Tensor, 
     if context_lens.numel() != B or seq_lens.numel() != B:
         raise ValueError("context_lens and seq_lens must have one entry per table row")
     dev = block_tables.device
+    _same_device(dev, context_lens=context_lens, seq_lens=seq_lens)
     if out is None:
         out = StepInputs(B, W, B if capacity is None else capacity, dev)
+    _same_device(dev, slot_mapping=out.slot_mapping, step_block_tables=out.block_tables)
     with torch.cuda.device(dev):
         st = lib.aeg_prepare_step_inputs(block_tables.data_ptr(), W, context_lens.data_ptr(), seq_lens.data_ptr(), B,
                                          out.slot_mapping.data_ptr(), out.positions.data_ptr(), out.capacity,
@@ -487,6 +498,7 @@ def reshape_and_cache_flash(key: torch.Tensor, value: torch.Tensor, key_cache: t
         raise NotImplementedError("only 2-byte cache elements (fp16/bf16) are supported")
     slot_mapping = slot_mapping.contiguous()
     dev = key_cache.device
+    _same_device(dev, key=key, value=value, value_cache=value_cache, slot_mapping=slot_mapping)
     with torch.cuda.device(dev):
         st = lib.aeg_reshape_and_cache(key.data_ptr(), value.data_ptr(), key.stride(0), value.stride(0),
                                        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0),
@@ -541,6 +553,7 @@ class DecodePlan:
             raise ValueError(f"block_tables must be int32 [{self.batch}, W]")
         if block_tables.size(1) == 0:
             raise ValueError("block_tables has no columns")
+        _same_device(self.device, seq_lens=seq_lens, block_tables=block_tables)
         seq_lens = seq_lens.contiguous()
         if block_tables.stride(1) != 1:
             block_tables = block_tables.contiguous()
@@ -625,6 +638,8 @@ def flash_attn_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache:
         raise ValueError("plan was built for a different batch / head layout / block tables / sequence lengths")
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     dev = query.device
+    _same_device(dev, key_cache=key_cache, value_cache=value_cache, block_table=block_table,
+                 cache_seqlens=cache_seqlens, out=out, plan_workspace=plan.workspace)
     with torch.cuda.device(dev):
         st = lib.aeg_paged_attn_decode(out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
                                        key_cache.data_ptr(), value_cache.data_ptr(), key_cache.stride(0),
@@ -687,6 +702,8 @@ def decode_layer_flash(query: torch.Tensor, key: torch.Tensor, value: torch.Tens
         raise ValueError("plan was built for a different batch / head layout / block tables / sequence lengths")
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     dev = query.device
+    _same_device(dev, key=key, value=value, key_cache=key_cache, value_cache=value_cache, block_table=block_table,
+                 cache_seqlens=cache_seqlens, out=out, plan_workspace=plan.workspace)
     with torch.cuda.device(dev):
         st = lib.aeg_decode_layer(out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0), key.data_ptr(),
                                   key.stride(0), value.data_ptr(), value.stride(0), key_cache.data_ptr(),

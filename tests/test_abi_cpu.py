@@ -131,6 +131,21 @@ def test_ops_module_imports_and_fails_loudly_without_cuda():
         ops.swap([0], [1], False, kv, torch.zeros_like(kv))
 
 
+def test_operands_on_another_device_are_rejected():
+    """Every operand of a launch must live on the device the work runs on; the check reads only
+    each tensor's device, so it runs here with stand-ins for tensors on two GPUs."""
+    import types
+
+    import torch
+
+    from aegaeon_b200 import ops
+
+    on = lambda i: types.SimpleNamespace(device=torch.device("cuda", i))  # noqa: E731
+    ops._same_device(torch.device("cuda", 0), key=on(0), value=on(0), out=None)
+    with pytest.raises(ValueError, match="value is on cuda:1"):
+        ops._same_device(torch.device("cuda", 0), key=on(0), value=on(1))
+
+
 def test_migration_and_ipc_validation_on_host():
     lib = _native.lib
     p, _k1 = _fake()
