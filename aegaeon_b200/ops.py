@@ -137,6 +137,28 @@ def swap_sm(source_block_ids, target_block_ids, is_swap_in: bool, kv_cache: torc
     dst.record_stream(torch.cuda.current_stream(dev))
 
 
+def swap_batched(src: torch.Tensor, dst: torch.Tensor, is_swap_in: bool, kv_cache: torch.Tensor,
+                 kv_swap: torch.Tensor, engine: str = "dma") -> None:
+    """``swap`` for id lists already held as int64 tensors (no Python list conversion).
+
+    ``engine="dma"``: host (CPU) id tensors, read in place; one copy-engine transfer per run of
+    blocks adjacent on both sides, as ``swap``. ``engine="sm"``: ids on the device (or staged
+    there), one kernel over the mapped page-locked ``kv_swap``, as ``swap_sm``. Same stream and
+    completion rules as ``swap``.
+    """
+    for t, name in ((src, "src"), (dst, "dst")):
+        if not isinstance(t, torch.Tensor) or t.dtype != torch.int64:
+            raise ValueError(f"{name} must be an int64 tensor")
+    if engine == "sm":
+        swap_sm(src, dst, is_swap_in, kv_cache, kv_swap)
+        return
+    if engine != "dma":
+        raise ValueError(f"engine must be 'dma' or 'sm', not {engine!r}")
+    if src.device.type != "cpu" or dst.device.type != "cpu":
+        raise ValueError("engine='dma' reads the ids on the host: src and dst must be CPU tensors")
+    swap(src.contiguous(), dst.contiguous(), is_swap_in, kv_cache, kv_swap)
+
+
 def copy_blocks(src_ids, dst_ids, kv_cache: torch.Tensor) -> None:
     """``kv_cache[dst_ids[i]] = kv_cache[src_ids[i]]`` for whole multi-layer blocks (device to device)."""
     _require_cuda(kv_cache, "kv_cache")

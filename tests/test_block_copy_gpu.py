@@ -78,6 +78,31 @@ def test_swap_sm_bit_exact(cuda_device):
     assert np.array_equal(_u8(kv), d_ref)
 
 
+@pytest.mark.parametrize("engine", ["dma", "sm"])
+def test_swap_batched_matches_swap(cuda_device, engine):
+    """The tensor-id form: CPU int64 ids for the copy engines, device ids for the SM kernel."""
+    kv, host = _pools(64, 40, seed=2)
+    rng = np.random.default_rng(5)
+    src = torch.as_tensor(rng.permutation(64)[:30])
+    dst = torch.as_tensor(rng.permutation(40)[:30])
+    d_ref, h_ref = _u8(kv), _u8(host)
+    ids = (src, dst) if engine == "dma" else (src.to(cuda_device), dst.to(cuda_device))
+    ops.swap_batched(*ids, False, kv, host, engine=engine)
+    torch.cuda.synchronize()
+    orc.c_swap(d_ref, h_ref, src.numpy(), dst.numpy(), False)
+    assert np.array_equal(_u8(host), h_ref)
+    back = torch.as_tensor(rng.permutation(64)[:30])
+    ops.swap_batched(dst, back, True, kv, host, engine=engine)
+    torch.cuda.synchronize()
+    orc.c_swap(d_ref, h_ref, dst.numpy(), back.numpy(), True)
+    assert np.array_equal(_u8(kv), d_ref)
+    with pytest.raises(ValueError, match="int64"):
+        ops.swap_batched(dst.to(torch.int32), back, True, kv, host, engine=engine)
+    if engine == "dma":
+        with pytest.raises(ValueError, match="CPU tensors"):
+            ops.swap_batched(dst.to(cuda_device), back, True, kv, host, engine="dma")
+
+
 def test_swap_sm_rejects_pageable_host_pool(cuda_device):
     kv, host = _pools(8, 8, pin=False)
     with pytest.raises(ValueError, match="page-locked"):
