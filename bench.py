@@ -607,7 +607,8 @@ def other_configs_leg(device, peak: float, max_layers: int = 4) -> dict:
     GPU: each as a step graph (plan + fused cache write and attention per layer) of its layers, at
     most ``max_layers`` of them for cfg4 (its pool then holds those layers only: same blocks and
     bytes per launch), per layer = (step - plan) / layers, and as launches timed alone. Tokens/s
-    of a whole step follow as batch / (plan + layers x per-layer time)."""
+    of a whole step follow as batch / (plan + layers x per-layer time). Also the same step as the
+    reference's two calls per layer (cache write, then attention), relative to the fused one."""
     from aegaeon_b200 import ops, synth
     from aegaeon_b200.step import DecodeStep
 
@@ -624,26 +625,33 @@ def other_configs_leg(device, peak: float, max_layers: int = 4) -> dict:
         synth.fill_normal_(kv, cfg.value_std, cfg.seed)
         step = DecodeStep(kv, Hq, B, lay.width, scale)
         g = torch.Generator(device=device).manual_seed(cfg.seed + 17)
-        step.load_inputs(q=(torch.randn(step.q.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
-                         k_new=(torch.randn(step.k_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
-                         v_new=(torch.randn(step.v_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
-                         slot_mapping=torch.as_tensor(synth.new_token_slots(lay), device=device),
-                         block_tables=torch.as_tensor(lay.block_tables, device=device),
-                         seq_lens=torch.as_tensor(lay.seq_lens, device=device))
-        step.capture()
-        for _ in range(3):
-            step.replay()
+        inputs = dict(q=(torch.randn(step.q.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                      k_new=(torch.randn(step.k_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                      v_new=(torch.randn(step.v_new.shape, generator=g, device=device) * cfg.value_std).to(cfg.dtype),
+                      slot_mapping=torch.as_tensor(synth.new_token_slots(lay), device=device),
+                      block_tables=torch.as_tensor(lay.block_tables, device=device),
+                      seq_lens=torch.as_tensor(lay.seq_lens, device=device))
         stream = torch.cuda.current_stream(device)
         reps = 20
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(device)
-        a.record(stream)
-        for _ in range(reps):
-            step.replay()
-        b.record(stream)
-        torch.cuda.synchronize(device)
-        step_ms = a.elapsed_time(b) / reps
+
+        def step_graph_ms(st):
+            st.load_inputs(**inputs)
+            st.capture()
+            for _ in range(3):
+                st.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(device)
+            a.record(stream)
+            for _ in range(reps):
+                st.replay()
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            return a.elapsed_time(b) / reps
+
+        step_ms = step_graph_ms(step)
         assert torch.isfinite(step.out.float()).all(), f"non-finite {name} output"
+        # the reference's two calls per layer (cache write, then attention) as one step graph
+        unfused_ms = step_graph_ms(DecodeStep(kv, Hq, B, lay.width, scale, fused=False))
         plan_ms = statistics.median(_per_launch_ms([lambda: step.plan.plan(step.seq_lens, step.block_tables)] * 4,
                                                    device))
         fns = [lambda l=l: ops.decode_layer(step.out[l], step.q[l], step.k_new[l], step.v_new[l], kv, l,
@@ -663,6 +671,7 @@ def other_configs_leg(device, peak: float, max_layers: int = 4) -> dict:
             "frac_isolated_launch": lb / (iso_ms / 1e3) / 1e9 / peak,
             "plan_us": plan_ms * 1e3,
             "tokens_per_s": B / ((plan_ms + per_layer * cfg.num_layers) / 1e3),
+            "unfused_step_vs_fused": unfused_ms / step_ms,
         }
         del step, kv
         torch.cuda.empty_cache()
