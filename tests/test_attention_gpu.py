@@ -67,6 +67,23 @@ def test_long_and_short_sequences_split_and_merge(cuda_device):
     assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_very_large_batch_of_short_sequences(cuda_device, dtype):
+    """5000 sequences of 0..40 tokens (more than the plan keeps block counts for in shared
+    memory, and more (sequence, head) pairs than worker warps): within tolerance of the oracle,
+    zero rows for empty sequences, no device error."""
+    rng = np.random.default_rng(21)
+    seq_lens = rng.integers(0, 41, size=5000)
+    kv, q, tables, sl = decode_case(len(seq_lens), 8, 1, seq_lens, dtype, num_layers=1, seed=21)
+    ops.read_device_errors(cuda_device)
+    out = _run(kv, q, tables, sl)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) == 0
+    assert torch.all(out[torch.as_tensor(sl == 0, device=cuda_device)] == 0)
+    want = oracle_attention_layer(q, kv[:, 0, 0], kv[:, 0, 1], tables, sl, SCALE)
+    assert_attention_close(out, want, "5000 short sequences")
+
+
 def test_zero_length_sequence_gives_zero_row(cuda_device):
     seq_lens = [0, 20, 0, 1]
     kv, q, tables, sl = decode_case(4, 28, 4, seq_lens, torch.bfloat16, num_layers=1, seed=5, width=4)

@@ -43,9 +43,11 @@ def test_prefill_matches_oracle(cuda_device, dtype, Hq, Hkv):
     assert ops.read_device_errors(cuda_device) == 0
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_prefill_long_prompts_match_torch_fp32(cuda_device, dtype):
-    lens = [2048, 777, 1, 1500]
+@pytest.mark.parametrize("dtype,lens", [(torch.float16, [2048, 777, 1, 1500]), (torch.bfloat16, [2048, 777, 1, 1500]),
+                                        (torch.bfloat16, [8192, 5])])
+def test_prefill_long_prompts_match_torch_fp32(cuda_device, dtype, lens):
+    """Larger batches against torch fp32 SDPA per prompt, up to the longest prompt of the
+    workload's range (8192 tokens, 64 key tiles per query tile)."""
     Hq, Hkv = 28, 4
     q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 5)
     scale = 128 ** -0.5
