@@ -84,11 +84,15 @@ def test_very_large_batch_of_short_sequences(cuda_device, dtype):
     assert_attention_close(out, want, "5000 short sequences")
 
 
-def test_zero_length_sequence_gives_zero_row(cuda_device):
-    seq_lens = [0, 20, 0, 1]
-    kv, q, tables, sl = decode_case(4, 28, 4, seq_lens, torch.bfloat16, num_layers=1, seed=5, width=4)
+@pytest.mark.parametrize("seq_lens", [[0, 20, 0, 1], [0, 0, 0]])
+def test_zero_length_sequence_gives_zero_row(cuda_device, seq_lens):
+    """Empty sequences give zero rows, also when the whole batch is empty (a plan of no blocks)."""
+    kv, q, tables, sl = decode_case(len(seq_lens), 28, 4, seq_lens, torch.bfloat16, num_layers=1, seed=5, width=4)
+    ops.read_device_errors(cuda_device)
     out = _run(kv, q, tables, sl)
-    assert torch.all(out[0] == 0) and torch.all(out[2] == 0)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) == 0
+    assert torch.all(out[torch.as_tensor(sl == 0, device=cuda_device)] == 0)
     want = oracle_attention_layer(q, kv[:, 0, 0], kv[:, 0, 1], tables, sl, SCALE)
     assert_attention_close(out, want, "zero-length")
 
