@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from aegaeon_b200 import ops, synth
-from aegaeon_b200._native import (AEG_DEVERR_BLOCK_ID_RANGE, AEG_DEVERR_SEQ_LEN_RANGE)
+from aegaeon_b200._native import (AEG_DEVERR_BLOCK_ID_RANGE, AEG_DEVERR_SEQ_LEN_RANGE, AEG_DEVERR_WAIT_TIMEOUT)
 from tests.gpu_helpers import assert_attention_close, decode_case, oracle_attention_layer
 
 pytestmark = pytest.mark.gpu
@@ -82,6 +82,55 @@ def test_very_large_batch_of_short_sequences(cuda_device, dtype):
     assert torch.all(out[torch.as_tensor(sl == 0, device=cuda_device)] == 0)
     want = oracle_attention_layer(q, kv[:, 0, 0], kv[:, 0, 1], tables, sl, SCALE)
     assert_attention_close(out, want, "5000 short sequences")
+
+
+def _first_warp_flag_offset(B: int, Hkv: int) -> int:
+    """Byte offset of worker warp 0's publication flag in a DecodePlan workspace: a 256-byte
+    header, then the warp records (three 16-byte records for each of the 4096 worker warps the
+    workspace is sized for, plus one) and the split-pair entries (16 bytes per (sequence, KV
+    head) pair), each region rounded up to 256 bytes."""
+    def up(x):
+        return (x + 255) & ~255
+    return up(up(256 + 3 * 16 * (4096 + 1)) + 16 * B * Hkv)
+
+
+def test_merge_wait_runs_out_and_reports(cuda_device):
+    """Failure detection without a fault: worker warp 0's publication flag is set to a value that
+    no launch stamps, as if that warp had never published its pieces, so the merges that need
+    them wait until their bounded wait (2 s) runs out. The launch reports
+    AEG_DEVERR_WAIT_TIMEOUT and returns, the context stays usable, and the next plan and launch
+    give the right output."""
+    import time
+
+    seq_lens = [3000, 40, 700, 5]  # the first pair spans many worker warps, warp 0 among them
+    B, Hq, Hkv = len(seq_lens), 28, 4
+    kv, q, tables, sl = decode_case(B, Hq, Hkv, seq_lens, torch.float16, num_layers=1, seed=13)
+    t_dev = torch.as_tensor(tables, device=cuda_device)
+    s_dev = torch.as_tensor(sl, device=cuda_device)
+    want = oracle_attention_layer(q, kv[:, 0, 0], kv[:, 0, 1], tables, sl, SCALE)
+    plan = ops.DecodePlan(B, Hq, Hkv, 128, cuda_device).plan(s_dev, t_dev)
+    ops.read_device_errors(cuda_device)
+    out = torch.full_like(q, float("nan"))
+    ops.paged_attention_decode(out, q, kv, 0, t_dev, s_dev, SCALE, plan=plan)  # every flag now holds 1
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) == 0
+    assert_attention_close(out, want, "before")
+    off = _first_warp_flag_offset(B, Hkv)
+    flag = plan.workspace[off:off + 4].view(torch.int32)
+    assert int(flag.item()) == 1  # the offset holds a publication flag after one launch
+    flag.fill_(7)
+    t0 = time.perf_counter()
+    ops.paged_attention_decode(torch.empty_like(q), q, kv, 0, t_dev, s_dev, SCALE, plan=plan)
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert ops.read_device_errors(cuda_device) & AEG_DEVERR_WAIT_TIMEOUT
+    assert 1.5 < waited < 20, waited
+    plan.plan(s_dev, t_dev)  # a new plan starts every flag at zero again
+    out = torch.full_like(q, float("nan"))
+    ops.paged_attention_decode(out, q, kv, 0, t_dev, s_dev, SCALE, plan=plan)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) == 0
+    assert_attention_close(out, want, "after")
 
 
 @pytest.mark.parametrize("seq_lens", [[0, 20, 0, 1], [0, 0, 0]])
