@@ -4,6 +4,8 @@ The reference runs decode attention and the cache write through vLLM 0.5.1's Fla
 backend (un-vendored). ``tests/golden/make_golden.py`` ran the same kernel family from the
 installed vLLM (``reshape_and_cache_flash`` + ``vllm_flash_attn.flash_attn_varlen_func`` with a
 block table, FA2) on per-layer views of Aegaeon's interleaved cache and saved inputs/outputs.
+``tests/golden/make_step_inputs_golden.py`` ran the reference's own ``Worker._prepare_model_inputs``
+on seeded batches and saved its step inputs.
 """
 import hashlib
 import os
@@ -78,3 +80,18 @@ def test_prefill_oracle_matches_vllm(name):
     got = orc.np_prefill_attention(g["q"], g["k"], g["v"], g["cu_seqlens"], float(g["scale"]), dt)
     ok, err, excess = orc.compare_attention(g["out_vllm"], got, dt, rtol=1e-2 if dt == orc.FP16 else 2e-2)
     assert ok, (err, excess)
+
+
+def test_step_inputs_oracle_matches_reference_code():
+    """The step-input oracle against the reference's own ``Worker._prepare_model_inputs`` and
+    ``make_tensor_with_pad``, run on seeded batches by ``tests/golden/make_step_inputs_golden.py``:
+    slot mapping, positions, query and sequence start offsets and the padded table rows, exactly."""
+    g = _load("step_inputs_reference.npz")
+    for k in range(int(g["cases"])):
+        seq, ctx = g[f"c{k}_seq_lens"].tolist(), g[f"c{k}_context_lens"].tolist()
+        off, flat = g[f"c{k}_table_offsets"], g[f"c{k}_tables_flat"]
+        tables = [flat[off[i]:off[i + 1]].tolist() for i in range(len(seq))]
+        got = orc.np_step_inputs(seq, ctx, tables)
+        for name in ("slot_mapping", "positions", "query_start_loc", "seq_start_loc", "block_tables"):
+            assert np.array_equal(got[name], g[f"c{k}_{name}"]), (k, name)
+        assert int(got["query_lens"].max()) == int(g[f"c{k}_max_query_len"])
