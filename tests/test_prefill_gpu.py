@@ -65,6 +65,24 @@ def test_prefill_long_prompts_match_torch_fp32(cuda_device, dtype, lens):
         assert bool(((got - ref).abs() <= tol).all()), (b, float((got - ref).abs().max()))
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_many_tiny_prompts_match_oracle(cuda_device, dtype):
+    """600 prompts of 0..3 tokens and one of 300 (many (level, prompt) groups, most of them a
+    single partly filled query tile, and empty prompts the work counter skips)."""
+    rng = np.random.default_rng(17)
+    lens = rng.integers(0, 4, size=600).tolist() + [300]
+    Hq, Hkv = 8, 2
+    q, k, v, cu = _inputs(cuda_device, lens, Hq, Hkv, dtype, 19)
+    scale = 128 ** -0.5
+    ops.read_device_errors(cuda_device)
+    out = ops.flash_attn_varlen_prefill(q, k, v, cu, max(lens), scale)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(cuda_device) == 0
+    want = orc.np_prefill_attention(_bits(q), _bits(k), _bits(v), cu.cpu().numpy(), scale, DT[dtype])
+    ok, err, excess = orc.compare_attention(_bits(out), want, DT[dtype])
+    assert ok, (err, excess)
+
+
 def test_prefill_work_counter_repeats_and_streams(cuda_device):
     """The kernel's CTAs take (level, prompt, head) items from a per-launch counter; the host
     rotates over 64 counter slots and each launch's last CTA resets its slot. More than 64
